@@ -1,0 +1,191 @@
+// C ABI entry points: argument validation, kernel choice, the unfused
+// "with reordering" forward and library identity.  See include/bsattn_b200.h.
+#include <math.h>
+
+#include "common.cuh"
+#include "internal.h"
+
+using namespace bsa;
+
+namespace {
+
+int check_device() {
+  static int cached[64];  // 0 unknown, 1 ok, 2 not sm_100
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess) return BSA_ERR_CUDA;
+  if (dev < 0 || dev >= 64) return BSA_ERR_DEVICE;
+  if (!cached[dev]) {
+    int major = 0, minor = 0;
+    if (cudaDeviceGetAttribute(&major, cudaDevAttrComputeCapabilityMajor, dev) != cudaSuccess ||
+        cudaDeviceGetAttribute(&minor, cudaDevAttrComputeCapabilityMinor, dev) != cudaSuccess)
+      return BSA_ERR_CUDA;
+    cached[dev] = (major == 10 && minor == 0) ? 1 : 2;
+  }
+  return cached[dev] == 1 ? BSA_OK : BSA_ERR_DEVICE;
+}
+
+bool valid_tensor(const bsa_tensor4d& t) { return t.data && t.stride_b >= 0 && t.stride_h >= 0 && t.stride_n >= 0; }
+
+int validate_fwd(const bsa_fwd_args* a) {
+  if (!a) return BSA_ERR_INVALID_ARG;
+  if (a->B <= 0 || a->H <= 0 || a->N <= 0 || a->D <= 0) return BSA_ERR_INVALID_ARG;
+  if (!dtype_bytes(a->dtype)) return BSA_ERR_DTYPE;
+  if (!valid_tensor(a->q) || !valid_tensor(a->k) || !valid_tensor(a->v) || !valid_tensor(a->o))
+    return BSA_ERR_INVALID_ARG;
+  if (!a->plan.tile_ptr || !a->plan.tile_col) return BSA_ERR_INVALID_ARG;
+  if (a->plan.block != 64 && a->plan.block != 128) return BSA_ERR_UNSUPPORTED;
+  if (a->plan.nb != (a->N + a->plan.block - 1) / a->plan.block) return BSA_ERR_SHAPE;
+  if (!(a->plan.mask_b == 1 || a->plan.mask_b == a->B)) return BSA_ERR_SHAPE;
+  if (!(a->plan.mask_h == 1 || a->plan.mask_h == a->H)) return BSA_ERR_SHAPE;
+  if (!(a->sm_scale > 0.f) || !isfinite(a->sm_scale)) return BSA_ERR_UNSUPPORTED;
+  if (a->kernel < BSA_KERNEL_AUTO || a->kernel > BSA_KERNEL_TCGEN05) return BSA_ERR_INVALID_ARG;
+  if (static_cast<int64_t>(a->B) * a->H > 65535) return BSA_ERR_UNSUPPORTED;  // grid.y
+  return BSA_OK;
+}
+
+bool simt_supported(const bsa_fwd_args* a) { return a->D == 16 || a->D == 32 || a->D == 64 || a->D == 128; }
+
+size_t round256(size_t x) { return (x + 255) & ~size_t(255); }
+
+// Workspace layout of bsa_fwd_reordered, 256-byte aligned regions:
+//   [q'] [k' v'] [o' lse'] -- q', o', lse' when q_perm is given, k', v' when kv_perm is.
+struct ReorderLayout {
+  size_t q, k, v, o, lse, total;
+};
+
+ReorderLayout reorder_layout(const bsa_fwd_args* a, bool has_q, bool has_kv) {
+  const size_t tensor = round256(static_cast<size_t>(a->B) * a->H * a->N * a->D * dtype_bytes(a->dtype));
+  const size_t lse = round256(static_cast<size_t>(a->B) * a->H * a->N * sizeof(float));
+  ReorderLayout L{};
+  size_t off = 0;
+  if (has_q) {
+    L.q = off;
+    off += tensor;
+  }
+  if (has_kv) {
+    L.k = off;
+    off += tensor;
+    L.v = off;
+    off += tensor;
+  }
+  if (has_q) {
+    L.o = off;
+    off += tensor;
+    if (a->lse) {
+      L.lse = off;
+      off += lse;
+    }
+  }
+  L.total = off;
+  return L;
+}
+
+bsa_tensor4d contiguous(void* base, const bsa_fwd_args* a) {
+  bsa_tensor4d t;
+  t.data = base;
+  t.stride_n = a->D;
+  t.stride_h = static_cast<int64_t>(a->N) * a->D;
+  t.stride_b = static_cast<int64_t>(a->H) * a->N * a->D;
+  return t;
+}
+
+}  // namespace
+
+extern "C" int bsa_abi_version(void) { return BSA_ABI_VERSION; }
+
+extern "C" const char* bsa_status_string(int status) {
+  switch (status) {
+    case BSA_OK: return "ok";
+    case BSA_ERR_INVALID_ARG: return "invalid argument";
+    case BSA_ERR_SHAPE: return "inconsistent shapes";
+    case BSA_ERR_DTYPE: return "unsupported dtype";
+    case BSA_ERR_ALIGNMENT: return "pointer or stride not 16-byte aligned";
+    case BSA_ERR_UNSUPPORTED: return "unsupported configuration";
+    case BSA_ERR_NOT_PERMUTATION: return "not a permutation";
+    case BSA_ERR_TIMEOUT: return "device wait timed out";
+    case BSA_ERR_CUDA: return "CUDA runtime error";
+    case BSA_ERR_WORKSPACE: return "workspace missing or too small";
+    case BSA_ERR_DEVICE: return "device is not sm_100 (B200)";
+    default: return "unknown status";
+  }
+}
+
+extern "C" int bsa_device_supported(int device, int* supported) {
+  if (!supported) return BSA_ERR_INVALID_ARG;
+  int major = 0, minor = 0;
+  if (cudaDeviceGetAttribute(&major, cudaDevAttrComputeCapabilityMajor, device) != cudaSuccess ||
+      cudaDeviceGetAttribute(&minor, cudaDevAttrComputeCapabilityMinor, device) != cudaSuccess) {
+    cudaGetLastError();
+    *supported = 0;
+    return BSA_ERR_CUDA;
+  }
+  *supported = (major == 10 && minor == 0) ? 1 : 0;
+  return BSA_OK;
+}
+
+extern "C" int bsa_fwd(const bsa_fwd_args* a, void* stream) {
+  int rc = validate_fwd(a);
+  if (rc) return rc;
+  if ((rc = check_device())) return rc;
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  const bool tc_ok = attn_tc_supported(a);
+  switch (a->kernel) {
+    case BSA_KERNEL_TCGEN05: return tc_ok ? launch_attn_tc(a, st) : BSA_ERR_UNSUPPORTED;
+    case BSA_KERNEL_SIMT: return simt_supported(a) ? launch_attn_simt(a, st) : BSA_ERR_UNSUPPORTED;
+    default:
+      if (tc_ok) return launch_attn_tc(a, st);
+      return simt_supported(a) ? launch_attn_simt(a, st) : BSA_ERR_UNSUPPORTED;
+  }
+}
+
+extern "C" int bsa_fwd_reordered_workspace_bytes(const bsa_fwd_args* a, size_t* bytes) {
+  if (!a || !bytes) return BSA_ERR_INVALID_ARG;
+  const int rc = validate_fwd(a);
+  if (rc) return rc;
+  *bytes = reorder_layout(a, true, true).total;
+  return BSA_OK;
+}
+
+extern "C" int bsa_fwd_reordered(const bsa_fwd_args* a, const void* q_perm, const void* kv_perm, int32_t perm_dtype,
+                                 void* workspace, size_t workspace_bytes, void* stream) {
+  int rc = validate_fwd(a);
+  if (rc) return rc;
+  if ((rc = check_device())) return rc;
+  if ((q_perm || kv_perm) && perm_dtype != BSA_INDEX_I32 && perm_dtype != BSA_INDEX_I64) return BSA_ERR_DTYPE;
+  const ReorderLayout L = reorder_layout(a, q_perm != nullptr, kv_perm != nullptr);
+  if (L.total && (!workspace || workspace_bytes < L.total)) return BSA_ERR_WORKSPACE;
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  uint8_t* ws = static_cast<uint8_t*>(workspace);
+  const int eb = dtype_bytes(a->dtype);
+  bsa_fwd_args inner = *a;
+  if (q_perm) {
+    inner.q = contiguous(ws + L.q, a);
+    if ((rc = launch_permute_rows(inner.q, a->q, a->B, a->H, a->N, a->D, eb, q_perm, perm_dtype, 0, a->err_flag, st)))
+      return rc;
+    inner.o = contiguous(ws + L.o, a);
+    if (a->lse) inner.lse = reinterpret_cast<float*>(ws + L.lse);
+  }
+  if (kv_perm) {
+    inner.k = contiguous(ws + L.k, a);
+    inner.v = contiguous(ws + L.v, a);
+    if ((rc = launch_permute_rows(inner.k, a->k, a->B, a->H, a->N, a->D, eb, kv_perm, perm_dtype, 0, a->err_flag,
+                                  st)))
+      return rc;
+    if ((rc = launch_permute_rows(inner.v, a->v, a->B, a->H, a->N, a->D, eb, kv_perm, perm_dtype, 0, a->err_flag,
+                                  st)))
+      return rc;
+  }
+  if ((rc = bsa_fwd(&inner, stream))) return rc;
+  if (q_perm) {
+    if ((rc = launch_permute_rows(a->o, inner.o, a->B, a->H, a->N, a->D, eb, q_perm, perm_dtype, 1, a->err_flag, st)))
+      return rc;
+    if (a->lse) {
+      // lse is a contiguous [B, H, N] fp32 array: rows of one element.
+      bsa_tensor4d dst{a->lse, static_cast<int64_t>(a->H) * a->N, a->N, 1};
+      bsa_tensor4d src{inner.lse, static_cast<int64_t>(a->H) * a->N, a->N, 1};
+      if ((rc = launch_permute_rows(dst, src, a->B, a->H, a->N, 1, 4, q_perm, perm_dtype, 1, a->err_flag, st)))
+        return rc;
+    }
+  }
+  return BSA_OK;
+}

@@ -1,0 +1,41 @@
+// Launchers shared between the translation units of the library.
+#pragma once
+
+#include <cuda_runtime.h>
+#include <stddef.h>
+#include <stdint.h>
+
+#include "../../include/bsattn_b200.h"
+
+namespace bsa {
+
+// Element size in bytes of a bsa_dtype (0 when invalid).
+inline int dtype_bytes(int dt) {
+  return dt == BSA_DTYPE_F32 ? 4 : (dt == BSA_DTYPE_F16 || dt == BSA_DTYPE_BF16) ? 2 : 0;
+}
+
+inline int tiles_per_row(int nb, int block) { return (nb * block + 127) / 128; }
+
+// preprocess.cu
+int launch_plan_count(const uint8_t* mask, int64_t sb, int64_t sh, int64_t srow, int mask_b, int mask_h, int nb,
+                      int block, int32_t* counts, cudaStream_t st);
+int launch_plan_scan(const int32_t* counts, int64_t n, int32_t* tile_ptr, cudaStream_t st);
+int launch_plan_fill(const uint8_t* mask, int64_t sb, int64_t sh, int64_t srow, int mask_b, int mask_h, int nb,
+                     int block, const int32_t* tile_ptr, int32_t* tile_col, cudaStream_t st);
+int launch_permute_rows(bsa_tensor4d dst, bsa_tensor4d src, int B, int H, int N, int row_elems, int elt_bytes,
+                        const void* perm, int perm_dtype, int inverse, int32_t* err, cudaStream_t st);
+
+// attn_simt.cu
+int launch_attn_simt(const bsa_fwd_args* a, cudaStream_t st);
+
+// attn_tc.cu
+bool attn_tc_supported(const bsa_fwd_args* a);
+int launch_attn_tc(const bsa_fwd_args* a, cudaStream_t st);
+
+}  // namespace bsa
+
+#define BSA_CUDA_CHECK(expr)                    \
+  do {                                          \
+    cudaError_t e_ = (expr);                    \
+    if (e_ != cudaSuccess) return BSA_ERR_CUDA; \
+  } while (0)

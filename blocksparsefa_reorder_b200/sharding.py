@@ -1,0 +1,88 @@
+"""Multi-GPU partitioning: independent (b, h) units spread over ranks.
+
+Every (b, h) pair of the forward is independent (the mask may differ per
+(b, h); the permutation applies per token), so the work shards into
+contiguous ranges of the flattened ``b * H + h`` index with no collective on
+the hot path.  One process per GPU (``torchrun``); each rank runs the
+single-GPU kernel on its own units.  Where a caller wants the full output on
+one rank, :func:`gather_units` collects the shards with point-to-point
+sends over the process group (NCCL over NVLink on B200, gloo on CPU).
+"""
+
+from __future__ import annotations
+
+from typing import Optional, Sequence
+
+import torch
+import torch.distributed as dist
+
+
+def partition_units(num_units: int, world_size: int, weights: Optional[Sequence[float]] = None) -> list:
+    """Split ``range(num_units)`` into ``world_size`` contiguous ``(lo, hi)``
+    ranges.  Without weights the sizes differ by at most one; with per-unit
+    weights (e.g. kept blocks per (b, h)) rank r's range ends at the last unit
+    whose cumulative weight is within ``(r + 1) / world_size`` of the total,
+    and the last rank takes the rest."""
+    if world_size <= 0:
+        raise ValueError("world_size must be positive")
+    if num_units < 0:
+        raise ValueError("num_units must be non-negative")
+    if weights is None:
+        base, extra = divmod(num_units, world_size)
+        out, lo = [], 0
+        for r in range(world_size):
+            hi = lo + base + (1 if r < extra else 0)
+            out.append((lo, hi))
+            lo = hi
+        return out
+    if len(weights) != num_units:
+        raise ValueError("one weight per unit")
+    if any(w < 0 for w in weights):
+        raise ValueError("weights must be non-negative")
+    total = float(sum(weights))
+    cum, acc = [], 0.0
+    for w in weights:
+        acc += float(w)
+        cum.append(acc)
+    out, lo = [], 0
+    for r in range(world_size):
+        if r == world_size - 1:
+            hi = num_units
+        else:
+            target = total * (r + 1) / world_size
+            hi = lo
+            while hi < num_units and cum[hi] <= target + 1e-9 * max(1.0, total):
+                hi += 1
+        out.append((lo, hi))
+        lo = hi
+    return out
+
+
+def local_heads(H: int, rank: int, world_size: int) -> tuple:
+    """Head range ``[h0, h1)`` of this rank when heads are sharded (B = 1)."""
+    return partition_units(H, world_size)[rank]
+
+
+def gather_units(local: torch.Tensor, ranges: Sequence[tuple], dst: int = 0, group=None) -> Optional[torch.Tensor]:
+    """Collect per-rank shards ``[hi - lo, ...]`` (rank r holds units
+    ``ranges[r]``) into one ``[total, ...]`` tensor on rank ``dst``; other
+    ranks return ``None``.  Every rank takes the same send/recv steps."""
+    rank = dist.get_rank(group)
+    world = dist.get_world_size(group)
+    if len(ranges) != world:
+        raise ValueError("one range per rank")
+    lo, hi = ranges[rank]
+    if local.shape[0] != hi - lo:
+        raise ValueError(f"rank {rank}: local shard has {local.shape[0]} units, expected {hi - lo}")
+    total = ranges[-1][1]
+    if rank == dst:
+        full = torch.empty((total,) + tuple(local.shape[1:]), dtype=local.dtype, device=local.device)
+        full[lo:hi].copy_(local)
+        for r in range(world):
+            rlo, rhi = ranges[r]
+            if r != dst and rhi > rlo:
+                dist.recv(full[rlo:rhi], src=r, group=group)
+        return full
+    if hi > lo:
+        dist.send(local.contiguous(), dst=dst, group=group)
+    return None

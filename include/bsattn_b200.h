@@ -1,0 +1,172 @@
+/*
+ * bsattn_b200.h -- C ABI of the B200 (sm_100a) block-sparse attention forward.
+ *
+ * Drop-in boundary for the hot path of KutayTasci/BlockSparseFA_Reorder:
+ * q, k, v [B,H,N,D] + a BLOCK x BLOCK block mask (+ optional token
+ * permutations) in, attention output in original token order out.
+ *
+ * Conventions
+ *  - Every pointer is a device pointer unless stated otherwise.  The library
+ *    never allocates device memory: scratch space is passed in as a
+ *    workspace whose size a *_sizes / *_workspace_bytes query returns.
+ *  - Every entry point is enqueued on `stream` (a cudaStream_t passed as
+ *    void*; NULL = legacy default stream) and does not synchronise.
+ *  - Return value: a bsa_status code (0 = success).  Nothing aborts.
+ *  - Permutation convention (reference utils.py:163-164, main.py:27-28):
+ *    perm[i] is the OLD index that moves to NEW position i.
+ *  - Tensors are 4-D [B, H, N, D] views given by a base pointer and element
+ *    strides for b, h and n; the innermost (D) stride must be 1.
+ */
+#ifndef BSATTN_B200_H
+#define BSATTN_B200_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#if defined(__GNUC__)
+#define BSA_API __attribute__((visibility("default")))
+#else
+#define BSA_API
+#endif
+
+#define BSA_ABI_VERSION 1
+
+typedef enum bsa_status {
+  BSA_OK = 0,
+  BSA_ERR_INVALID_ARG = 1,     /* null pointer / non-positive size / bad enum      */
+  BSA_ERR_SHAPE = 2,           /* inconsistent shapes (mask vs N, strides, ...)    */
+  BSA_ERR_DTYPE = 3,           /* unsupported element type                         */
+  BSA_ERR_ALIGNMENT = 4,       /* pointer or stride not 16-byte aligned (TMA)      */
+  BSA_ERR_UNSUPPORTED = 5,     /* head dim / block size / scale not supported      */
+  BSA_ERR_NOT_PERMUTATION = 6, /* device check found a value out of range / dup    */
+  BSA_ERR_TIMEOUT = 7,         /* a bounded device wait ran out (err flag)         */
+  BSA_ERR_CUDA = 8,            /* CUDA runtime error (launch / attribute)          */
+  BSA_ERR_WORKSPACE = 9,       /* workspace missing or too small                   */
+  BSA_ERR_DEVICE = 10          /* current device is not sm_100                     */
+} bsa_status;
+
+typedef enum bsa_dtype { BSA_DTYPE_F32 = 0, BSA_DTYPE_F16 = 1, BSA_DTYPE_BF16 = 2 } bsa_dtype;
+typedef enum bsa_index_dtype { BSA_INDEX_I32 = 0, BSA_INDEX_I64 = 1 } bsa_index_dtype;
+
+/* Kernel choice for bsa_fwd (AUTO picks tcgen05 for f16/bf16 with D in
+ * {64,128} and BLOCK in {64,128}, the SIMT kernel otherwise). */
+typedef enum bsa_kernel { BSA_KERNEL_AUTO = 0, BSA_KERNEL_SIMT = 1, BSA_KERNEL_TCGEN05 = 2 } bsa_kernel;
+
+/* Bits that kernels OR into the optional device error word (int32). */
+#define BSA_DEVERR_TIMEOUT 1     /* bounded mbarrier wait ran out                 */
+#define BSA_DEVERR_PERM_RANGE 2  /* permutation value outside [0, n)              */
+#define BSA_DEVERR_PERM_DUP 4    /* permutation value repeated                    */
+#define BSA_DEVERR_COORD 8       /* coordinate negative or outside the perm      */
+#define BSA_DEVERR_PLAN 16       /* plan entry outside [0, nb)                    */
+
+typedef struct bsa_tensor4d {
+  void* data;
+  int64_t stride_b, stride_h, stride_n; /* in elements; stride_d == 1 */
+} bsa_tensor4d;
+
+/* Per-tile list of kept key blocks (output of bsa_build_plan).  A tile is
+ * 128 query rows: one block row for BLOCK 128, block rows 2t and 2t+1 for
+ * BLOCK 64.  Tiles of mask slice s = (mask_b==1 ? 0 : b) * mask_h +
+ * (mask_h==1 ? 0 : h) are tile_ptr[s*T + t] .. tile_ptr[s*T + t + 1] in
+ * tile_col, T = ceil(nb * BLOCK / 128).  Each entry is (flags << 24) |
+ * key_block, ascending in key_block; flags bit 0 / bit 1 = the first /
+ * second block row of the tile keeps that key block. */
+typedef struct bsa_plan {
+  const int32_t* tile_ptr;
+  const int32_t* tile_col;
+  int32_t mask_b, mask_h;
+  int32_t nb;    /* ceil(N / block) */
+  int32_t block; /* 64 or 128 */
+} bsa_plan;
+
+typedef struct bsa_fwd_args {
+  int32_t B, H, N, D;
+  int32_t dtype;            /* bsa_dtype of q, k, v and o                         */
+  bsa_tensor4d q, k, v, o;
+  float sm_scale;           /* softmax scale, > 0 (reference: 1/sqrt(D))          */
+  float* lse;               /* optional contiguous [B,H,N] fp32 LSE in log2 units
+                               (the reference's M); NULL = not written            */
+  bsa_plan plan;
+  int32_t* err_flag;        /* optional device int32 for BSA_DEVERR_* bits        */
+  int32_t kernel;           /* bsa_kernel                                         */
+} bsa_fwd_args;
+
+/* Library identity. */
+BSA_API int bsa_abi_version(void);
+BSA_API const char* bsa_status_string(int status);
+/* 1 in *supported when `device` is an sm_100 part the kernels were built for. */
+BSA_API int bsa_device_supported(int device, int* supported);
+
+/* Sizes for a plan over a [mask_b, mask_h, nb, nb] mask: tile_ptr length,
+ * tile_col capacity (worst case: every block kept) and workspace bytes. */
+BSA_API int bsa_plan_sizes(int32_t mask_b, int32_t mask_h, int32_t nb, int32_t block, int64_t* tile_ptr_len,
+                           int64_t* tile_col_capacity, size_t* workspace_bytes);
+
+/* Block mask (bytes, nonzero = kept, [mask_b, mask_h, nb, nb] with the given
+ * element strides) -> per-tile CSR.  Replaces the per-query-block scan of
+ * every mask byte inside the reference kernel
+ * (triton_kernels/BlockSparse_Naive.py:25-32, BlockSparse_Fused.py:29-35). */
+BSA_API int bsa_build_plan(const uint8_t* mask, int64_t stride_b, int64_t stride_h, int64_t stride_row,
+                           int32_t mask_b, int32_t mask_h, int32_t nb, int32_t block, int32_t* tile_ptr,
+                           int32_t* tile_col, void* workspace, size_t workspace_bytes, void* stream);
+
+/* Attention forward on tensors already in the mask's token order.
+ * Replaces _attn_fwd_block_sparse (triton_kernels/BlockSparse_Naive.py:68-125)
+ * as launched at BlockSparseTriton_Naive.py:142-156: o = softmax over kept
+ * blocks of (q k^T * sm_scale) v; rows that keep no block give o = 0 and
+ * lse = -inf. */
+BSA_API int bsa_fwd(const bsa_fwd_args* args, void* stream);
+
+/* Row gather / scatter along N for every (b, h); D = elements per row:
+ *   inverse == 0: dst[b,h,i,:] = src[b,h,perm[i],:]
+ *     (apply_reordering, utils.py:260-266; torch.gather at
+ *      BlockSparseTriton_Naive.py:89-97)
+ *   inverse != 0: dst[b,h,perm[i],:] = src[b,h,i,:]
+ *     (reverse_reordering, utils.py:269-288; scatter_ at
+ *      BlockSparseTriton_Naive.py:158-161)
+ * Out-of-range perm values set BSA_DEVERR_PERM_RANGE and skip the row. */
+BSA_API int bsa_permute_rows(bsa_tensor4d dst, bsa_tensor4d src, int32_t B, int32_t H, int32_t N, int32_t D,
+                             int32_t dtype, const void* perm, int32_t perm_dtype, int32_t inverse,
+                             int32_t* err_flag, void* stream);
+
+/* inv[perm[i]] = i with validation (utils.py:253-254, 283-284; the checks of
+ * read_reordering_file_to_tensor, utils.py:222-231): out-of-range values set
+ * BSA_DEVERR_PERM_RANGE, repeated values BSA_DEVERR_PERM_DUP. */
+BSA_API int bsa_inverse_permutation(const void* perm, int32_t perm_dtype, int64_t n, int64_t* inv_out,
+                                    int32_t* err_flag, void* stream);
+
+/* out[i] = inv_perm[idx[i]]  (update_idx_perm, utils.py:236-258, given the
+ * inverse permutation).  Indices outside [0, n) set BSA_DEVERR_COORD and
+ * copy the index unchanged. */
+BSA_API int bsa_remap_indices(const int64_t* idx, int64_t count, const int64_t* inv_perm, int64_t n,
+                              int64_t* out, int32_t* err_flag, void* stream);
+
+/* Token coordinates -> bool block mask [B, H, nb, nb] (uint8 0/1, contiguous),
+ * nb = ceil(seq_len / block); coordinates whose block index is >= nb are
+ * dropped, negative ones set BSA_DEVERR_COORD.  The same mask is written to
+ * every (b, h).  `row_inv` / `col_inv` (optional, length seq_len) remap the
+ * coordinates through inverse permutations first, fusing update_idx_perm.
+ * Replaces generate_blockmask_from_mtx_coords (utils.py:51-84). */
+BSA_API int bsa_blockmask_from_coords(const int64_t* rows, const int64_t* cols, int64_t count, int64_t seq_len,
+                                      int32_t block, int32_t B, int32_t H, const int64_t* row_inv,
+                                      const int64_t* col_inv, uint8_t* mask_out, int32_t* err_flag,
+                                      void* stream);
+
+/* "With reordering" forward, unfused: gather q by q_perm and k, v by kv_perm
+ * into the workspace, run bsa_fwd with the mask in the new order, scatter o
+ * (and lse) back by q_perm.  Either permutation may be NULL (identity).
+ * Mirrors the timed loop of BlockSparseTriton_Naive.py:129-161.  `args->o`
+ * and `args->lse` receive results in ORIGINAL order. */
+BSA_API int bsa_fwd_reordered_workspace_bytes(const bsa_fwd_args* args, size_t* bytes);
+BSA_API int bsa_fwd_reordered(const bsa_fwd_args* args, const void* q_perm, const void* kv_perm,
+                              int32_t perm_dtype, void* workspace, size_t workspace_bytes, void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* BSATTN_B200_H */

@@ -1,0 +1,244 @@
+"""Parity of the CUDA attention forward (tcgen05 and SIMT kernels) against the
+CPU oracle and against the reference kernels' own outputs (golden vectors).
+
+Tolerances (fixed by the parity spec): max |err| <= 2e-2 for bf16 / fp16
+against the float64 masked-softmax definition, <= 1e-5 for fp32; exactly
+zero contribution from key blocks outside the mask.
+"""
+
+import math
+
+import numpy as np
+import pytest
+import torch
+
+from blocksparsefa_reorder_b200 import BlockSparsePlan, block_sparse_attention
+from blocksparsefa_reorder_b200 import kernels as K
+from blocksparsefa_reorder_b200 import workloads as W
+from oracle import attention as OA
+
+pytestmark = pytest.mark.gpu
+
+TOL_16 = 2e-2
+TOL_32 = 1e-5
+TOL_LSE = 2e-2
+
+
+def _rand_mask(nb, p, seed, shape=(1, 1), empty_rows=()):
+    rng = np.random.default_rng(seed)
+    m = rng.random(shape + (nb, nb)) < p
+    idx = np.arange(nb)
+    m[..., idx, idx] = True
+    for r in empty_rows:
+        m[..., r, :] = False
+    return m
+
+
+def _qkv(B, H, N, D, dtype, seed, dev, scale=1.0):
+    g = torch.Generator(device="cpu").manual_seed(seed)
+    ts = [(torch.randn(B, H, N, D, generator=g) * scale).to(dtype) for _ in range(3)]
+    return [t.to(dev) for t in ts]
+
+
+def _oracle(q, k, v, mask, block, q_perm=None, kv_perm=None, sm_scale=None):
+    f = lambda t: t.float().cpu().numpy()  # noqa: E731
+    qp = None if q_perm is None else q_perm.cpu().numpy()
+    kp = None if kv_perm is None else kv_perm.cpu().numpy()
+    return OA.reordered_attention(f(q), f(k), f(v), mask, block, qp, kp, sm_scale)
+
+
+def _maxerr(o, ref):
+    return float(np.abs(o.float().cpu().numpy().astype(np.float64) - ref).max())
+
+
+@pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float16])
+@pytest.mark.parametrize("D", [64, 128])
+@pytest.mark.parametrize("block", [128, 64])
+def test_tcgen05_matches_oracle(dev, dtype, D, block):
+    B, H, N = 1, 2, 1024
+    nb = N // block
+    mask = _rand_mask(nb, 0.3, seed=D + block, shape=(1, H), empty_rows=(3,))
+    q, k, v = _qkv(B, H, N, D, dtype, seed=7, dev=dev)
+    o, lse = block_sparse_attention(q, k, v, torch.from_numpy(mask).to(dev), return_lse=True, kernel="tcgen05",
+                                    check_errors=True)
+    ref, ref_lse = _oracle(q, k, v, mask, block)
+    assert _maxerr(o, ref) <= TOL_16
+    lv = lse.cpu().numpy()
+    fin = np.isfinite(ref_lse)
+    assert np.array_equal(np.isfinite(lv), fin)
+    assert np.abs(lv[fin] - ref_lse[fin]).max() <= TOL_LSE
+    # the empty block row gives exactly zero and lse = -inf
+    assert torch.count_nonzero(o[:, :, 3 * block:4 * block]) == 0
+    assert np.all(np.isneginf(lv[:, :, 3 * block:4 * block]))
+
+
+@pytest.mark.parametrize("D,block", [(64, 64), (128, 64), (64, 128), (128, 128)])
+def test_tcgen05_repeatable(dev, D, block):
+    """Pipeline races show up as run-to-run differences: 25 runs of the same
+    call into NaN-prefilled outputs must be bitwise identical and in tolerance.
+    The masks include tiles whose trailing key blocks are kept by only one of
+    the two block rows of a 128-row tile (BLOCK 64), the pattern that exposed
+    an epilogue ordering bug."""
+    B, H, N = 1, 2, 1024
+    mask = _rand_mask(N // block, 0.3, seed=D + block, shape=(1, H), empty_rows=(3,))
+    q, k, v = _qkv(B, H, N, D, torch.bfloat16, seed=7, dev=dev)
+    plan = BlockSparsePlan(torch.from_numpy(mask).to(dev), block)
+    ref, _ = _oracle(q, k, v, mask, block)
+    first = None
+    for _ in range(25):
+        o = torch.full_like(q, float("nan"))
+        block_sparse_attention(q, k, v, plan=plan, kernel="tcgen05", out=o)
+        if first is None:
+            first = o.clone()
+            assert _maxerr(first, ref) <= TOL_16
+        assert torch.equal(o, first)
+
+
+def test_fp32_simt_plumbing_config(dev):
+    wl = W.make("plumbing")
+    q, k, v = wl.make_qkv(dev)
+    o = block_sparse_attention(q, k, v, wl.mask_tensor(dev), block=wl.block, check_errors=True)
+    ref, _ = _oracle(q, k, v, wl.mask[None, None], wl.block)
+    assert _maxerr(o, ref) <= TOL_32
+
+
+@pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float16])
+def test_permuted_path_matches_oracle(dev, dtype):
+    B, H, N, D, block = 2, 2, 1024, 128, 128
+    nb = N // block
+    mask = _rand_mask(nb, 0.4, seed=5)
+    q, k, v = _qkv(B, H, N, D, dtype, seed=9, dev=dev)
+    g = torch.Generator().manual_seed(3)
+    qp = torch.randperm(N, generator=g).to(dev)
+    kp = torch.randperm(N, generator=g).to(dev)
+    o, lse = block_sparse_attention(q, k, v, torch.from_numpy(mask).to(dev), q_perm=qp, kv_perm=kp,
+                                    return_lse=True, check_errors=True)
+    ref, ref_lse = _oracle(q, k, v, mask, block, qp, kp)
+    assert _maxerr(o, ref) <= TOL_16
+    assert np.abs(lse.cpu().numpy() - ref_lse).max() <= TOL_LSE
+
+
+def test_golden_reference_kernels(dev, golden_dir):
+    """Our kernels against the reference Triton kernels' outputs, through the
+    kernel-level drop-ins called like the reference runners call Triton."""
+    g = np.load(golden_dir / "attention_golden.npz")
+    for name in g["names"]:
+        B, H, N, D, BL = (int(x) for x in g[f"{name}_meta"])
+        q, k, v = (torch.from_numpy(g[f"{name}_{t}"]).to(dev) for t in "qkv")
+        bm = torch.from_numpy(g[f"{name}_mask"]).to(dev)
+        M = torch.empty(B, H, N, dtype=torch.float32, device=dev)
+        o = torch.empty_like(q)
+        sc = 1.0 / math.sqrt(D)
+        if f"{name}_q_perm" in g:
+            qp = torch.from_numpy(g[f"{name}_q_perm"]).to(dev)
+            kp = torch.from_numpy(g[f"{name}_kv_perm"]).to(dev)
+            rp = qp.view(1, 1, N, 1).expand(B, H, N, D)
+            cp = kp.view(1, 1, N, 1).expand(B, H, N, D)
+            K.attn_fwd_block_sparse_perm(sc, M, B, H, q, k, v, o, bm, N_CTX=N, q_perm=rp, kv_perm=cp, HEAD_DIM=D,
+                                         BLOCK_M=BL, BLOCK_N=BL, STAGE=1, warp_specialize=False, IS_HOPPER=False,
+                                         num_warps=4, num_stages=3)
+        else:
+            K.attn_fwd_block_sparse(sc, M, B, H, q, k, v, o, bm, N_CTX=N, HEAD_DIM=D, BLOCK_M=BL, BLOCK_N=BL,
+                                    STAGE=1, warp_specialize=False, IS_HOPPER=False, num_warps=4, num_stages=3)
+        ref_o = g[f"{name}_o"].astype(np.float64)
+        ref_M = g[f"{name}_M"]
+        assert np.abs(o.float().cpu().numpy() - ref_o).max() <= TOL_16, name
+        m = M.cpu().numpy()
+        fin = np.isfinite(ref_M)
+        assert np.array_equal(np.isfinite(m), fin), name
+        assert np.abs(m[fin] - ref_M[fin]).max() <= TOL_LSE, name
+
+
+@pytest.mark.parametrize("block", [128, 64])
+def test_masked_blocks_contribute_nothing(dev, block):
+    """NaN/Inf-poison every K/V row in key blocks that no query block keeps,
+    and perturb them: O must stay finite and bitwise equal."""
+    B, H, N, D = 1, 2, 1024, 128
+    nb = N // block
+    mask = _rand_mask(nb, 0.2, seed=21)
+    mask[..., :, nb - 2:] = False
+    unused = np.nonzero(~mask[0, 0].any(axis=0))[0]
+    assert unused.size > 0
+    q, k, v = _qkv(B, H, N, D, torch.bfloat16, seed=4, dev=dev)
+    mt = torch.from_numpy(mask).to(dev)
+    o1 = block_sparse_attention(q, k, v, mt)
+    k2, v2 = k.clone(), v.clone()
+    for j in unused:
+        k2[:, :, j * block:(j + 1) * block] = float("nan")
+        v2[:, :, j * block:(j + 1) * block] = float("inf")
+    o2 = block_sparse_attention(q, k2, v2, mt)
+    assert torch.isfinite(o2.float()).all()
+    assert torch.equal(o1, o2)
+    # finite perturbation of every K/V row outside the kept blocks of the
+    # first tile row block leaves that block row bitwise unchanged
+    k3, v3 = k.clone(), v.clone()
+    for j in np.nonzero(~mask[0, 0, 0])[0]:
+        k3[:, :, j * block:(j + 1) * block] += 3.0
+        v3[:, :, j * block:(j + 1) * block] -= 5.0
+    o3 = block_sparse_attention(q, k3, v3, mt)
+    if block == 128:
+        assert torch.equal(o1[:, :, :block], o3[:, :, :block])
+
+
+def test_tcgen05_vs_simt_crosscheck(dev):
+    B, H, N, D, block = 1, 2, 2048, 128, 128
+    mask = _rand_mask(N // block, 0.25, seed=8)
+    q, k, v = _qkv(B, H, N, D, torch.bfloat16, seed=12, dev=dev)
+    mt = torch.from_numpy(mask).to(dev)
+    a = block_sparse_attention(q, k, v, mt, kernel="tcgen05")
+    b = block_sparse_attention(q, k, v, mt, kernel="simt")
+    assert (a.float() - b.float()).abs().max().item() <= TOL_16
+
+
+def test_strided_bnhd_layout(dev):
+    """q, k, v as [B, N, H, D] memory viewed as [B, H, N, D] (the layout the
+    reference's BSFA runner uses, BlockSparseFA.py:28-34): TMA takes the
+    strides directly, no copy."""
+    B, H, N, D, block = 2, 3, 512, 64, 128
+    mask = _rand_mask(N // block, 0.5, seed=30)
+    base = [torch.randn(B, N, H, D, generator=torch.Generator().manual_seed(i)).to(torch.bfloat16).to(dev)
+            for i in range(3)]
+    q, k, v = (t.permute(0, 2, 1, 3) for t in base)
+    o = block_sparse_attention(q, k, v, torch.from_numpy(mask).to(dev), kernel="tcgen05")
+    ref, _ = _oracle(q, k, v, mask, block)
+    assert _maxerr(o, ref) <= TOL_16
+
+
+def test_partial_last_tile(dev):
+    """N = 64 * odd with BLOCK 64: the last 128-row tile has one block row;
+    TMA zero-fills the missing rows and clips the store."""
+    B, H, N, D, block = 1, 2, 64 * 9, 128, 64
+    mask = _rand_mask(N // block, 0.4, seed=31, shape=(1, H))
+    q, k, v = _qkv(B, H, N, D, torch.float16, seed=3, dev=dev)
+    o = block_sparse_attention(q, k, v, torch.from_numpy(mask).to(dev), kernel="tcgen05", check_errors=True)
+    ref, _ = _oracle(q, k, v, mask, block)
+    assert _maxerr(o, ref) <= TOL_16
+
+
+def test_per_batch_head_masks(dev):
+    B, H, N, D, block = 2, 3, 1024, 128, 128
+    mask = _rand_mask(N // block, 0.3, seed=40, shape=(B, H))
+    q, k, v = _qkv(B, H, N, D, torch.bfloat16, seed=41, dev=dev)
+    o = block_sparse_attention(q, k, v, torch.from_numpy(mask).to(dev), check_errors=True)
+    ref, _ = _oracle(q, k, v, mask, block)
+    assert _maxerr(o, ref) <= TOL_16
+
+
+def test_headline_full_size_sampled(dev):
+    """Full-size headline workload (B1 H16 N16384 D128 bf16, 10% blocks):
+    sampled query blocks against the oracle's block loop; a second run is
+    bitwise identical (deterministic)."""
+    wl = W.make("headline")
+    q, k, v = wl.make_qkv(dev)
+    plan = BlockSparsePlan(wl.mask_tensor(dev), wl.block)
+    o = block_sparse_attention(q, k, v, plan=plan, check_errors=True)
+    o2 = block_sparse_attention(q, k, v, plan=plan)
+    assert torch.equal(o, o2)
+    heads = [0, 15]
+    qblocks = [0, 37, 127]
+    sub = lambda t: t[:, heads].float().cpu().numpy()  # noqa: E731
+    ref, _ = OA.block_sparse_online(sub(q), sub(k), sub(v), wl.mask[None, None], wl.block, query_blocks=qblocks)
+    got = o[:, heads].float().cpu().numpy()
+    for mb in qblocks:
+        r0, r1 = mb * wl.block, (mb + 1) * wl.block
+        assert np.abs(got[:, :, r0:r1] - ref[:, :, r0:r1]).max() <= TOL_16
