@@ -24,6 +24,7 @@ INDEX_I32, INDEX_I64 = 0, 1
 KERNEL_AUTO, KERNEL_SIMT, KERNEL_TCGEN05 = 0, 1, 2
 DEVERR_TIMEOUT, DEVERR_PERM_RANGE, DEVERR_PERM_DUP, DEVERR_COORD, DEVERR_PLAN = 1, 2, 4, 8, 16
 ABI_VERSION = 1
+PLAN_NOALLOC_MAX_TILES = 1 << 20
 
 
 class Tensor4d(ctypes.Structure):
@@ -59,6 +60,7 @@ PROTOS = {
     "bsa_plan_sizes": ([_i32, _i32, _i32, _i32, ctypes.POINTER(_i64), ctypes.POINTER(_i64), ctypes.POINTER(_sz)],
                        ctypes.c_int),
     "bsa_build_plan": ([_vp, _i64, _i64, _i64, _i32, _i32, _i32, _i32, _vp, _vp, _vp, _sz, _vp], ctypes.c_int),
+    "bsa_build_plan_noalloc": ([_vp, _i64, _i64, _i64, _i32, _i32, _i32, _i32, _vp, _vp, _vp], ctypes.c_int),
     "bsa_fwd": ([ctypes.POINTER(FwdArgs), _vp], ctypes.c_int),
     "bsa_permute_rows": ([Tensor4d, Tensor4d, _i32, _i32, _i32, _i32, _i32, _vp, _i32, _i32, _vp, _vp],
                          ctypes.c_int),

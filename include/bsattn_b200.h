@@ -114,6 +114,23 @@ BSA_API int bsa_build_plan(const uint8_t* mask, int64_t stride_b, int64_t stride
                            int32_t mask_b, int32_t mask_h, int32_t nb, int32_t block, int32_t* tile_ptr,
                            int32_t* tile_col, void* workspace, size_t workspace_bytes, void* stream);
 
+/* bsa_build_plan for callers that may not allocate device memory (a host
+ * framework that owns every device buffer through its own pool, a serving
+ * loop that cannot afford an allocation's implicit synchronisation).  No
+ * counterpart in the reference.  Same inputs and outputs as bsa_build_plan
+ * minus the workspace: the per-tile scratch lives in a fixed device array
+ * inside the library (BSA_PLAN_NOALLOC_MAX_TILES int32 = 4 MiB, held by every
+ * GPU that loads the library until exit).  Returns BSA_ERR_WORKSPACE when the
+ * mask has more than BSA_PLAN_NOALLOC_MAX_TILES tiles (mask_b * mask_h *
+ * ceil(nb * block / 128)).  The first call on a device looks the array's
+ * address up (cudaGetSymbolAddress), so make it before any stream capture.
+ * Calls share the array: calls that overlap on the GPU race and must be
+ * serialised by the caller.  Allocates nothing. */
+#define BSA_PLAN_NOALLOC_MAX_TILES (1 << 20)
+BSA_API int bsa_build_plan_noalloc(const uint8_t* mask, int64_t stride_b, int64_t stride_h, int64_t stride_row,
+                                   int32_t mask_b, int32_t mask_h, int32_t nb, int32_t block, int32_t* tile_ptr,
+                                   int32_t* tile_col, void* stream);
+
 /* Attention forward on tensors already in the mask's token order.
  * Replaces _attn_fwd_block_sparse (triton_kernels/BlockSparse_Naive.py:68-125)
  * as launched at BlockSparseTriton_Naive.py:142-156: o = softmax over kept
