@@ -150,10 +150,10 @@ extern "C" int bsa_fwd_reordered(const bsa_fwd_args* a, const void* q_perm, cons
                                  void* workspace, size_t workspace_bytes, void* stream) {
   int rc = validate_fwd(a);
   if (rc) return rc;
-  if ((rc = check_device())) return rc;
   if ((q_perm || kv_perm) && perm_dtype != BSA_INDEX_I32 && perm_dtype != BSA_INDEX_I64) return BSA_ERR_DTYPE;
   const ReorderLayout L = reorder_layout(a, q_perm != nullptr, kv_perm != nullptr);
   if (L.total && (!workspace || workspace_bytes < L.total)) return BSA_ERR_WORKSPACE;
+  if ((rc = check_device())) return rc;
   cudaStream_t st = static_cast<cudaStream_t>(stream);
   uint8_t* ws = static_cast<uint8_t*>(workspace);
   const int eb = dtype_bytes(a->dtype);

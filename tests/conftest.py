@@ -30,6 +30,17 @@ def pytest_collection_modifyitems(config, items):
             item.add_marker(skip)
 
 
+@pytest.fixture(scope="session", autouse=True)
+def built_library():
+    """Build the CUDA extension once if it is missing (nvcc cross-compiles
+    without a GPU); an existing build is used as is."""
+    from blocksparsefa_reorder_b200 import build
+
+    if not build.LIB_PATH.exists():
+        build.build()
+    return build.LIB_PATH
+
+
 @pytest.fixture(scope="session")
 def golden_dir():
     return GOLDEN

@@ -1,0 +1,94 @@
+"""Multi-rank logic on CPU with the gloo backend (world size 2).
+
+The GPU path shards (b, h) units across ranks with no collective; here each
+rank computes its units with the CPU oracle (standing in for the GPU kernel,
+which these CPU ranks cannot run) and rank 0 gathers the shards with
+gather_units.  A failure test makes one rank raise before the gather and
+checks that the other rank's receive ends with an error within the process
+group's timeout instead of hanging."""
+
+import os
+import socket
+import traceback
+from datetime import timedelta
+
+import numpy as np
+import torch
+import torch.distributed as dist
+import torch.multiprocessing as mp
+
+from blocksparsefa_reorder_b200 import sharding
+from oracle import attention as OA
+
+
+def _free_port():
+    s = socket.socket()
+    s.bind(("127.0.0.1", 0))
+    port = s.getsockname()[1]
+    s.close()
+    return port
+
+
+def _init(rank, world, port, timeout_s=30):
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    dist.init_process_group("gloo", rank=rank, world_size=world, timeout=timedelta(seconds=timeout_s))
+
+
+def _worker_shard(rank, world, port, out_dir):
+    try:
+        _init(rank, world, port)
+        B, H, N, D, block = 1, 4, 256, 32, 64
+        g = np.random.default_rng(0)
+        q, k, v = (g.standard_normal((B, H, N, D)).astype(np.float32) for _ in range(3))
+        mask = g.random((1, 1, N // block, N // block)) < 0.5
+        ranges = sharding.partition_units(B * H, world)
+        lo, hi = ranges[rank]
+        o, _ = OA.block_sparse_online(q, k, v, mask, block, heads=list(range(lo, hi)))
+        local = torch.from_numpy(o.reshape(B * H, N, D)[lo:hi].copy())
+        full = sharding.gather_units(local, ranges, dst=0)
+        if rank == 0:
+            ref, _ = OA.block_sparse_online(q, k, v, mask, block)
+            np.save(os.path.join(out_dir, "err.npy"), np.array([np.abs(full.numpy() - ref.reshape(B * H, N, D)).max()]))
+        dist.barrier()
+        dist.destroy_process_group()
+    except Exception:
+        with open(os.path.join(out_dir, f"fail{rank}.txt"), "w") as f:
+            f.write(traceback.format_exc())
+        raise
+
+
+def test_sharded_units_gather_to_rank0(tmp_path):
+    port = _free_port()
+    mp.start_processes(_worker_shard, args=(2, port, str(tmp_path)), nprocs=2, join=True, start_method="spawn")
+    err = np.load(tmp_path / "err.npy")[0]
+    assert err == 0.0
+
+
+def _worker_fail(rank, world, port, out_dir):
+    _init(rank, world, port, timeout_s=5)
+    if rank == 1:
+        # a rank that fails between steps, before its send
+        os._exit(3)
+    buf = torch.zeros(4)
+    try:
+        dist.recv(buf, src=1)
+        ok = "received"
+    except Exception as e:  # the peer is gone: the receive must fail, not hang
+        ok = "error: " + type(e).__name__
+    with open(os.path.join(out_dir, "rank0.txt"), "w") as f:
+        f.write(ok)
+    os._exit(0)
+
+
+def test_rank_failure_is_detected_not_hung(tmp_path):
+    port = _free_port()
+    ctx = mp.start_processes(_worker_fail, args=(2, port, str(tmp_path)), nprocs=2, join=False,
+                             start_method="spawn")
+    for p in ctx.processes:
+        p.join(timeout=60)
+    alive = [p for p in ctx.processes if p.is_alive()]
+    for p in alive:
+        p.kill()
+    assert not alive, "a rank hung after its peer died"
+    assert (tmp_path / "rank0.txt").read_text().startswith("error")
