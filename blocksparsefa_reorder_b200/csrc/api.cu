@@ -47,6 +47,8 @@ bool simt_supported(const bsa_fwd_args* a) { return a->D == 16 || a->D == 32 || 
 
 size_t round256(size_t x) { return (x + 255) & ~size_t(255); }
 
+int launch_tc(const bsa_fwd_args* a, cudaStream_t st) { return launch_attn_tc(a, st); }
+
 // Workspace layout of bsa_fwd_reordered, 256-byte aligned regions:
 //   [q'] [k' v'] [o' lse'] -- q', o', lse' when q_perm is given, k', v' when kv_perm is.
 struct ReorderLayout {
@@ -130,10 +132,10 @@ extern "C" int bsa_fwd(const bsa_fwd_args* a, void* stream) {
   cudaStream_t st = static_cast<cudaStream_t>(stream);
   const bool tc_ok = attn_tc_supported(a);
   switch (a->kernel) {
-    case BSA_KERNEL_TCGEN05: return tc_ok ? launch_attn_tc(a, st) : BSA_ERR_UNSUPPORTED;
+    case BSA_KERNEL_TCGEN05: return tc_ok ? launch_tc(a, st) : BSA_ERR_UNSUPPORTED;
     case BSA_KERNEL_SIMT: return simt_supported(a) ? launch_attn_simt(a, st) : BSA_ERR_UNSUPPORTED;
     default:
-      if (tc_ok) return launch_attn_tc(a, st);
+      if (tc_ok) return launch_tc(a, st);
       return simt_supported(a) ? launch_attn_simt(a, st) : BSA_ERR_UNSUPPORTED;
   }
 }

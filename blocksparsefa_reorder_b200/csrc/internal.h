@@ -32,6 +32,7 @@ int launch_attn_simt(const bsa_fwd_args* a, cudaStream_t st);
 bool attn_tc_supported(const bsa_fwd_args* a);
 int launch_attn_tc(const bsa_fwd_args* a, cudaStream_t st);
 
+
 }  // namespace bsa
 
 #define BSA_CUDA_CHECK(expr)                    \

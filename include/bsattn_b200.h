@@ -62,6 +62,7 @@ typedef enum bsa_kernel { BSA_KERNEL_AUTO = 0, BSA_KERNEL_SIMT = 1, BSA_KERNEL_T
 #define BSA_DEVERR_PERM_DUP 4    /* permutation value repeated                    */
 #define BSA_DEVERR_COORD 8       /* coordinate negative or outside the perm      */
 #define BSA_DEVERR_PLAN 16       /* plan entry outside [0, nb)                    */
+#define BSA_DEVERR_ALIGN 32      /* dynamic shared memory not 1024-byte aligned   */
 
 typedef struct bsa_tensor4d {
   void* data;
