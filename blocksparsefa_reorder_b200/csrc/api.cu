@@ -47,7 +47,10 @@ bool simt_supported(const bsa_fwd_args* a) { return a->D == 16 || a->D == 32 || 
 
 size_t round256(size_t x) { return (x + 255) & ~size_t(255); }
 
-int launch_tc(const bsa_fwd_args* a, cudaStream_t st) { return launch_attn_tc(a, st); }
+// The persistent kernel (one CTA per SM looping over tiles) overlaps one
+// tile's epilogue with the next tile's start; attn_tc.cu is its one-tile-per-
+// CTA form.
+int launch_tc(const bsa_fwd_args* a, cudaStream_t st) { return launch_attn_tcp(a, st); }
 
 // Workspace layout of bsa_fwd_reordered, 256-byte aligned regions:
 //   [q'] [k' v'] [o' lse'] -- q', o', lse' when q_perm is given, k', v' when kv_perm is.

@@ -37,6 +37,7 @@
 
 #include "common.cuh"
 #include "internal.h"
+#include "softmax.cuh"
 
 namespace bsa {
 
@@ -241,25 +242,23 @@ __global__ void __launch_bounds__(192, 1)
 #pragma unroll
       for (int c = 0; c < BN / 32; ++c) tmem_ld32(lane_base + (sb ? C::S_COL1 : C::S_COL0) + c * 32, &sr[c * 32]);
       tmem_wait_ld();
-      const uint32_t flags = static_cast<uint32_t>(__ldg(&p.tile_col[e0 + j])) >> 24;
+      const uint32_t entry = static_cast<uint32_t>(__ldg(&p.tile_col[e0 + j]));
+      const uint32_t flags = entry >> 24;
       const bool active = BN == 128 ? true : (((flags >> half) & 1u) != 0);
+      // keys at or past N (a partial last key block; TMA zero-filled them) are
+      // masked out: only the one block that crosses N takes this branch
+      {
+        const int kvalid = p.N - static_cast<int>(entry & 0xFFFFFFu) * BN;
+        if (kvalid < BN) {
+#pragma unroll
+          for (int i = 0; i < BN; ++i)
+            if (i >= kvalid) sr[i] = __float_as_uint(-INFINITY);
+        }
+      }
       uint32_t pr[BN / 2];
       if (active) {
-        float mx = __uint_as_float(sr[0]);
-#pragma unroll
-        for (int i = 1; i < BN; ++i) mx = fmaxf(mx, __uint_as_float(sr[i]));
-        const float m_new = fmaxf(m_run, mx * p.scale_log2);
-        float alpha = 1.f;
-        bool resc = false;
-        if (m_run == -INFINITY) {
-          m_run = m_new;
-        } else if (m_new - m_run > 8.f) {
-          alpha = ex2_approx(m_run - m_new);
-          l_run *= alpha;
-          m_run = m_new;
-          resc = true;
-        }
-        if (__any_sync(0xffffffffu, resc)) {
+        const float alpha = softmax_block<BN, BF16>(sr, pr, p.scale_log2, m_run, l_run);
+        if (__any_sync(0xffffffffu, alpha != 1.f)) {
           // O holds the sum up to block j-1: wait for PV_{j-1}, rescale in TMEM.
           if (!(ok = __all_sync(0xffffffffu, mbar_wait(pv_done, (j - 1) & 1, abort_flag, p.err)))) break;
           tc_fence_after();
@@ -273,16 +272,6 @@ __global__ void __launch_bounds__(192, 1)
             tmem_st32(lane_base + C::O_COL + c * 32, o);
           }
         }
-        const float neg_m = -m_run;
-        float ls = 0.f;
-#pragma unroll
-        for (int i = 0; i < BN / 2; ++i) {
-          const float p0 = ex2_approx(fmaf(__uint_as_float(sr[2 * i]), p.scale_log2, neg_m));
-          const float p1 = ex2_approx(fmaf(__uint_as_float(sr[2 * i + 1]), p.scale_log2, neg_m));
-          ls += p0 + p1;
-          pr[i] = pack2<BF16>(p0, p1);
-        }
-        l_run += ls;
       } else {
 #pragma unroll
         for (int i = 0; i < BN / 2; ++i) pr[i] = 0u;
@@ -348,44 +337,15 @@ __global__ void __launch_bounds__(192, 1)
 // ---------------------------------------------------------------------------
 // Host side
 // ---------------------------------------------------------------------------
-PFN_cuTensorMapEncodeTiled_v12000 get_encode_fn() {
-  static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
-  if (!fn) {
-    void* ptr = nullptr;
-    cudaDriverEntryPointQueryResult q;
-    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &ptr, cudaEnableDefault, &q) == cudaSuccess &&
-        q == cudaDriverEntryPointSuccess)
-      fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(ptr);
-  }
-  return fn;
-}
-
-// 4-D map over [B, H, N, D] (TMA order: D, N, H, B), box = 64 x rows, 128B swizzle.
-int make_map(CUtensorMap* m, const bsa_tensor4d& tdesc, int B, int H, int N, int D, bool bf16, int rows) {
-  auto enc = get_encode_fn();
-  if (!enc) return BSA_ERR_CUDA;
-  const cuuint64_t dims[4] = {static_cast<cuuint64_t>(D), static_cast<cuuint64_t>(N), static_cast<cuuint64_t>(H),
-                              static_cast<cuuint64_t>(B)};
-  const cuuint64_t strides[3] = {static_cast<cuuint64_t>(tdesc.stride_n) * 2,
-                                 static_cast<cuuint64_t>(tdesc.stride_h) * 2,
-                                 static_cast<cuuint64_t>(tdesc.stride_b) * 2};
-  const cuuint32_t box[4] = {64, static_cast<cuuint32_t>(rows), 1, 1};
-  const cuuint32_t estr[4] = {1, 1, 1, 1};
-  CUresult r = enc(m, bf16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 4, tdesc.data, dims,
-                   strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
-                   CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
-  return r == CUDA_SUCCESS ? BSA_OK : BSA_ERR_ALIGNMENT;
-}
-
 template <int D, int BN, bool BF16>
 int launch_cfg(const bsa_fwd_args* a, cudaStream_t st) {
   using C = TcCfg<D, BN>;
   CUtensorMap mq, mk, mv, mo;
   int r;
-  if ((r = make_map(&mq, a->q, a->B, a->H, a->N, D, BF16, 128))) return r;
-  if ((r = make_map(&mk, a->k, a->B, a->H, a->N, D, BF16, BN))) return r;
-  if ((r = make_map(&mv, a->v, a->B, a->H, a->N, D, BF16, BN))) return r;
-  if ((r = make_map(&mo, a->o, a->B, a->H, a->N, D, BF16, 128))) return r;
+  if ((r = make_tensor_map_4d(&mq, a->q, a->B, a->H, a->N, D, BF16, 128))) return r;
+  if ((r = make_tensor_map_4d(&mk, a->k, a->B, a->H, a->N, D, BF16, BN))) return r;
+  if ((r = make_tensor_map_4d(&mv, a->v, a->B, a->H, a->N, D, BF16, BN))) return r;
+  if ((r = make_tensor_map_4d(&mo, a->o, a->B, a->H, a->N, D, BF16, 128))) return r;
   TcParams p;
   p.tile_ptr = a->plan.tile_ptr;
   p.tile_col = a->plan.tile_col;
@@ -411,6 +371,39 @@ bool aligned16(const bsa_tensor4d& t) {
 }
 
 }  // namespace
+
+namespace {
+PFN_cuTensorMapEncodeTiled_v12000 get_encode_fn() {
+  static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+  if (!fn) {
+    void* ptr = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &ptr, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(ptr);
+  }
+  return fn;
+}
+
+}  // namespace
+
+// 4-D map over [B, H, N, D] (TMA order: D, N, H, B), box = 64 x rows, 128B swizzle.
+int make_tensor_map_4d(CUtensorMap* m, const bsa_tensor4d& tdesc, int B, int H, int N, int D, bool bf16, int rows) {
+  auto enc = get_encode_fn();
+  if (!enc) return BSA_ERR_CUDA;
+  const cuuint64_t dims[4] = {static_cast<cuuint64_t>(D), static_cast<cuuint64_t>(N), static_cast<cuuint64_t>(H),
+                              static_cast<cuuint64_t>(B)};
+  const cuuint64_t strides[3] = {static_cast<cuuint64_t>(tdesc.stride_n) * 2,
+                                 static_cast<cuuint64_t>(tdesc.stride_h) * 2,
+                                 static_cast<cuuint64_t>(tdesc.stride_b) * 2};
+  const cuuint32_t box[4] = {64, static_cast<cuuint32_t>(rows), 1, 1};
+  const cuuint32_t estr[4] = {1, 1, 1, 1};
+  CUresult r = enc(m, bf16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 4, tdesc.data, dims,
+                   strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                   CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  return r == CUDA_SUCCESS ? BSA_OK : BSA_ERR_ALIGNMENT;
+}
+
 
 bool attn_tc_supported(const bsa_fwd_args* a) {
   if (a->dtype != BSA_DTYPE_F16 && a->dtype != BSA_DTYPE_BF16) return false;

@@ -1,6 +1,7 @@
 // Launchers shared between the translation units of the library.
 #pragma once
 
+#include <cuda.h>
 #include <cuda_runtime.h>
 #include <stddef.h>
 #include <stdint.h>
@@ -31,6 +32,11 @@ int launch_attn_simt(const bsa_fwd_args* a, cudaStream_t st);
 // attn_tc.cu
 bool attn_tc_supported(const bsa_fwd_args* a);
 int launch_attn_tc(const bsa_fwd_args* a, cudaStream_t st);
+// 4-D TMA map over a [B, H, N, D] 16-bit tensor, box 64 x rows, 128-byte swizzle.
+int make_tensor_map_4d(CUtensorMap* m, const bsa_tensor4d& t, int B, int H, int N, int D, bool bf16, int rows);
+
+// attn_tcp.cu: the same pipeline, persistent over tiles
+int launch_attn_tcp(const bsa_fwd_args* a, cudaStream_t st);
 
 
 }  // namespace bsa

@@ -242,3 +242,82 @@ def test_headline_full_size_sampled(dev):
     for mb in qblocks:
         r0, r1 = mb * wl.block, (mb + 1) * wl.block
         assert np.abs(got[:, :, r0:r1] - ref[:, :, r0:r1]).max() <= TOL_16
+
+
+def _torch_masked_reference(q, k, v, mask, block, sm_scale):
+    """fp32 masked softmax attention on the GPU, one (b, h) slice at a time:
+    rows with no kept key give O = 0 and lse = -inf."""
+    B, H, N, _ = q.shape
+    o = torch.zeros(B, H, N, q.shape[-1], dtype=torch.float32, device=q.device)
+    lse = torch.full((B, H, N), float("-inf"), dtype=torch.float32, device=q.device)
+    mt = torch.from_numpy(mask).to(q.device)
+    for b in range(B):
+        for h in range(H):
+            m = mt[b % mt.shape[0], h % mt.shape[1]]
+            full = m.repeat_interleave(block, 0).repeat_interleave(block, 1)[:N, :N]
+            s = (q[b, h].float() @ k[b, h].float().T) * sm_scale
+            s = s.masked_fill(~full, float("-inf"))
+            ls = torch.logsumexp(s, dim=-1)
+            p = torch.exp(s - ls[:, None].clamp_min(-1e30))
+            p = torch.where(full, p, torch.zeros_like(p))
+            o[b, h] = p @ v[b, h].float()
+            lse[b, h] = ls / math.log(2.0)  # the API's lse is in log2 units
+    return o, lse
+
+
+@pytest.mark.parametrize("D,block", [(64, 64), (128, 64), (64, 128), (128, 128)])
+def test_many_tiles_per_cta(dev, D, block):
+    """Several times more 128-row tiles than SMs, so each CTA of the
+    persistent kernel runs many tiles back to back: per-(b, h) masks with
+    empty block rows scattered through them and one head with no kept block
+    at all, a partial last tile, NaN-prefilled outputs, lse checked, and three
+    runs bitwise identical."""
+    B, H, N = 2, 8, 4096 - 64
+    nb = (N + block - 1) // block
+    mask = _rand_mask(nb, 0.2, seed=D * 7 + block, shape=(B, H))
+    rng = np.random.default_rng(D + block)
+    for r in rng.choice(nb, size=nb // 4, replace=False):
+        mask[rng.integers(B), rng.integers(H), r, :] = False
+    mask[1, 5] = False
+    q, k, v = _qkv(B, H, N, D, torch.bfloat16, seed=D + block, dev=dev)
+    plan = BlockSparsePlan(torch.from_numpy(mask).to(dev), block)
+    scale = 1.0 / math.sqrt(D)
+    ref_o, ref_lse = _torch_masked_reference(q, k, v, mask, block, scale)
+    first = None
+    for _ in range(3):
+        o = torch.full_like(q, float("nan"))
+        o, lse = block_sparse_attention(q, k, v, plan=plan, kernel="tcgen05", return_lse=True, out=o,
+                                        check_errors=True)
+        if first is None:
+            first = (o.clone(), lse.clone())
+            assert (o.float() - ref_o).abs().max().item() <= TOL_16
+            fin = torch.isfinite(ref_lse)
+            assert torch.equal(torch.isfinite(lse), fin)
+            assert (lse[fin] - ref_lse[fin]).abs().max().item() <= TOL_LSE
+            assert torch.count_nonzero(o[1, 5]) == 0
+        assert torch.equal(o, first[0]) and torch.equal(lse, first[1])
+
+
+@pytest.mark.parametrize("D,block", [(64, 64), (128, 64), (64, 128), (128, 128)])
+def test_reference_point_guard(dev, D, block):
+    """The kernels take a row's softmax reference point from its first kept
+    block and redo a block with the exact max only when its sum overflows
+    the slack: keys of one later block scaled by 30 force that path (scores
+    ~40 log2 units above the reference), and an earlier block scaled down
+    makes the first reference point low.  Checked against the float64
+    oracle, O and lse."""
+    B, H, N = 1, 2, 1024
+    nb = N // block
+    mask = _rand_mask(nb, 0.6, seed=D + block + 3, shape=(1, H))
+    mask[..., :, nb - 2] = True
+    q, k, v = _qkv(B, H, N, D, torch.bfloat16, seed=D + block, dev=dev)
+    k[:, :, (nb - 2) * block:(nb - 1) * block] *= 30
+    k[:, :, :block] *= 0.1
+    o, lse = block_sparse_attention(q, k, v, torch.from_numpy(mask).to(dev), return_lse=True, kernel="tcgen05",
+                                    check_errors=True)
+    ref, ref_lse = _oracle(q, k, v, mask, block)
+    assert _maxerr(o, ref) <= TOL_16
+    lv = lse.cpu().numpy()
+    fin = np.isfinite(ref_lse)
+    assert np.array_equal(np.isfinite(lv), fin)
+    assert np.abs(lv[fin] - ref_lse[fin]).max() <= TOL_LSE * max(1.0, float(np.abs(ref_lse[fin]).max()) / 8)
