@@ -23,7 +23,7 @@ DTYPE_F32, DTYPE_F16, DTYPE_BF16 = 0, 1, 2
 INDEX_I32, INDEX_I64 = 0, 1
 KERNEL_AUTO, KERNEL_SIMT, KERNEL_TCGEN05 = 0, 1, 2
 DEVERR_TIMEOUT, DEVERR_PERM_RANGE, DEVERR_PERM_DUP, DEVERR_COORD, DEVERR_PLAN = 1, 2, 4, 8, 16
-ABI_VERSION = 1
+ABI_VERSION = 2
 PLAN_NOALLOC_MAX_TILES = 1 << 20
 
 
@@ -34,7 +34,8 @@ class Tensor4d(ctypes.Structure):
 
 class Plan(ctypes.Structure):
     _fields_ = [("tile_ptr", ctypes.c_void_p), ("tile_col", ctypes.c_void_p), ("mask_b", ctypes.c_int32),
-                ("mask_h", ctypes.c_int32), ("nb", ctypes.c_int32), ("block", ctypes.c_int32)]
+                ("mask_h", ctypes.c_int32), ("nb", ctypes.c_int32), ("block", ctypes.c_int32),
+                ("tile_order", ctypes.c_void_p)]
 
 
 class FwdArgs(ctypes.Structure):
@@ -61,6 +62,7 @@ PROTOS = {
                        ctypes.c_int),
     "bsa_build_plan": ([_vp, _i64, _i64, _i64, _i32, _i32, _i32, _i32, _vp, _vp, _vp, _sz, _vp], ctypes.c_int),
     "bsa_build_plan_noalloc": ([_vp, _i64, _i64, _i64, _i32, _i32, _i32, _i32, _vp, _vp, _vp], ctypes.c_int),
+    "bsa_build_tile_order": ([_vp, _i32, _i32, _i32, _i32, _vp, _vp], ctypes.c_int),
     "bsa_fwd": ([ctypes.POINTER(FwdArgs), _vp], ctypes.c_int),
     "bsa_permute_rows": ([Tensor4d, Tensor4d, _i32, _i32, _i32, _i32, _i32, _vp, _i32, _i32, _vp, _vp],
                          ctypes.c_int),

@@ -80,8 +80,9 @@ class BlockSparsePlan:
     ``block_mask``: bool (or uint8) CUDA tensor ``[nb, nb]`` or
     ``[1|B, 1|H, nb, nb]``.  The plan replaces the reference kernel's scan of
     every mask byte (``BlockSparse_Naive.py:25-32``) and can be reused across
-    calls with the same mask.  Building it enqueues three small kernels and
-    does not synchronise.
+    calls with the same mask.  It also holds the work order the tcgen05
+    kernel hands tiles out in (each slice's tiles by decreasing kept-block
+    count).  Building it enqueues four small kernels and does not synchronise.
     """
 
     def __init__(self, block_mask: torch.Tensor, block: int):
@@ -110,6 +111,9 @@ class BlockSparsePlan:
         _lib.check(L.bsa_build_plan(m.data_ptr(), m.stride(0), m.stride(1), m.stride(2), self.mask_b, self.mask_h,
                                     self.nb, self.block, self.tile_ptr.data_ptr(), self.tile_col.data_ptr(),
                                     work.data_ptr(), ws.value, _stream(self.device)), "bsa_build_plan")
+        self.tile_order = torch.empty(max(1, ptr_len.value - 1), dtype=torch.int32, device=self.device)
+        _lib.check(L.bsa_build_tile_order(self.tile_ptr.data_ptr(), self.mask_b, self.mask_h, self.nb, self.block,
+                                          self.tile_order.data_ptr(), _stream(self.device)), "bsa_build_tile_order")
         self._mask_ref = m  # keep the mask alive until the kernels ran
         self._work = work
 
@@ -123,7 +127,7 @@ class BlockSparsePlan:
 
     def c_plan(self) -> _lib.Plan:
         return _lib.Plan(self.tile_ptr.data_ptr(), self.tile_col.data_ptr(), self.mask_b, self.mask_h, self.nb,
-                         self.block)
+                         self.block, self.tile_order.data_ptr())
 
 
 def _check_err(err: Optional[torch.Tensor], what: str) -> None:

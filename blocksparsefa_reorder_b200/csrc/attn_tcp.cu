@@ -1,35 +1,46 @@
 // Persistent tcgen05 block-sparse attention forward for sm_100a.
 //
-// The pipeline of attn_tc.cu (one 128-row query tile at a time: TMA
-// producer warp, one MMA-issuing thread, one softmax warpgroup, S
-// double-buffered in TMEM) run by one CTA per SM over many tiles, so that
-// one tile's epilogue and the next tile's start overlap instead of leaving
-// the tensor cores idle between CTAs.  Replaces _attn_fwd_block_sparse
-// (triton_kernels/BlockSparse_Naive.py:68-125); results are those of the
-// reference's online softmax (:39-60, 119-125): rows with no kept block give
-// O = 0 and lse = -inf.
+// Replaces _attn_fwd_block_sparse (triton_kernels/BlockSparse_Naive.py:68-125)
+// with its online softmax (:39-60) and epilogue (:119-125): rows with no kept
+// block give O = 0 and lse = -inf.  Keys at or past N (a partial last key
+// block) are masked.
 //
-// Work: CTA c takes tiles w = c, c + G, c + 2G, ... of the (b, h)-major tile
-// order (w = bh * T + t), so the CTAs in flight share a head's K / V in L2.
+// One CTA per SM loops over 128-row query tiles.  The tiles are numbered
+// w = bh * T + r in (b, h)-major order, r ranking the rows of the head's mask
+// slice by decreasing kept-block count (the plan's tile_order; natural order
+// without one), and CTAs claim them from a global counter: longest tiles
+// first within a head, dynamically, so the CTAs finish together, while the
+// CTAs in flight still share a head's K / V in L2.  The producer claims a
+// tile and passes its number to the other roles through a small ring in
+// shared memory.  The counter is one of kWorkSlots per device, taken in turn
+// by successive launches; the last CTA to finish resets it.  Roles:
+//  * warp 0, one thread: TMA producer (Q per tile, then K_g and V_g-1 per
+//    kept block, V one block behind K because PV_g-1 is issued after S_g);
+//  * warp 1, one thread: tcgen05.mma issuer (S_g = Q K_g^T, then PV_g-1);
+//  * warpgroup 1: softmax, one query row per thread, P written back into
+//    the first BN/2 columns of S's TMEM;
+//  * warpgroup 2: epilogue, one query row per thread: O / l from TMEM
+//    straight to global memory, lse, and the zero rows of empty tiles.
+// The epilogue has its own warps so that the softmax goes straight on to the
+// next tile while the previous tile's output is written.
 //
-// Across tiles:
-//  * block counter j runs on from tile to tile: S_j goes to TMEM buffer j&1
-//    and P_j is written back into the first columns of that buffer (the
-//    next S into the buffer is issued after the PV that reads P, and one
-//    thread's tcgen05.mma operations execute in issue order);
-//  * non-empty tiles alternate between two Q buffers in shared memory and
-//    two O accumulators in TMEM (counter e);
-//  * the MMA thread issues the last PV of a tile after the first S of the
-//    next, and waits for the epilogue to have read an O buffer (o_empty)
-//    before the first PV that overwrites it;
-//  * the epilogue stages O in the tile's Q buffer for the TMA store and
-//    releases that buffer to the producer (q_empty) once the store has read
-//    it, which is checked during the next tile's first block.
-// TMEM columns: S0 [0,BN), S1 [BN,2BN), O0 [2BN, 2BN+D), O1 [2BN+D, 2BN+2D).
-//
+// Buffers: S double-buffered in TMEM by global block counter g (S_g in
+// buffer g&1); O double-buffered by non-empty-tile counter e (O_e in buffer
+// e&1); Q double-buffered in shared memory by e; K and V in rings of KS and
+// VS stages.  TMEM columns: S0 [0,BN), S1 [BN,2BN), O0 [2BN,2BN+D),
+// O1 [2BN+D,2BN+2D).
+// Ordering facts (one thread's tcgen05.mma operations execute in issue order
+// and tcgen05.commit tracks every earlier one):
+//  * S_g+2 reuses S_g's TMEM and is issued after PV_g, which reads P_g there;
+//  * S_g complete implies PV_g-2 complete, and PV_g-1 completes before any
+//    later MMA: the softmax's rescale of O waits pv_done for PV_g-1;
+//  * Q_e's buffer is released (q_empty) by a commit after the tile's last S;
+//  * the first PV of tile e+2 waits o_empty[e&1]: the epilogue has read O_e.
 // Every wait is bounded by %globaltimer; a timeout sets BSA_DEVERR_TIMEOUT
 // and all roles drain and exit.
 #include <cudaTypedefs.h>
+
+#include <atomic>
 
 #include "common.cuh"
 #include "internal.h"
@@ -39,18 +50,37 @@ namespace bsa {
 
 namespace {
 
+// Tile counters for dynamic claiming: launch k uses slot k % kWorkSlots, so
+// up to kWorkSlots launches may run at the same time on different streams.
+constexpr int kWorkSlots = 64;
+__device__ uint32_t g_work_next[kWorkSlots];
+__device__ uint32_t g_work_done[kWorkSlots];
+
+constexpr int kTileRing = 8;   // tile numbers in flight between the producer and the other roles
+constexpr int kTileUsers = 9;  // MMA thread + 4 softmax warps + 4 epilogue warps
+
 struct TcpParams {
   const int32_t* tile_ptr;
   const int32_t* tile_col;
+  const int32_t* tile_order;  // optional: per slice, rows by decreasing kept-block count
   float* lse;
-  void* o_raw;  // for the zero rows of empty tiles (plain stores)
-  int64_t os_b, os_h, os_n;
+  uint8_t* o;                // output base (16-bit elements)
+  int64_t os_b, os_h, os_n;  // output strides in elements
   int32_t* err;
   int H, N, nb, T, mask_b, mask_h, total_tiles;
+  int slot;  // work counter slot
   float scale_log2;
 };
 
 constexpr int kSmemLimitP = 232448;
+constexpr int kThreadsP = 384;
+// setmaxnreg split over the three warpgroups; the launch holds 168 per thread
+// (65536 / 384 rounded down to a multiple of 8).
+constexpr int kRegsLaunchP = 168;
+constexpr int kRegsIssueP = 72;
+constexpr int kRegsSoftmaxP = 240;
+constexpr int kRegsEpilogueP = 96;
+static_assert(128 * (kRegsIssueP + kRegsSoftmaxP + kRegsEpilogueP) <= kThreadsP * kRegsLaunchP, "register split");
 
 template <int D, int BN>
 struct TcpCfg {
@@ -61,24 +91,25 @@ struct TcpCfg {
   static constexpr int Q_BYTES = BM * D * 2;
   static constexpr int KV_BYTES = BN * D * 2;
   static constexpr int BAR_BYTES = 512;
-  // K and V have their own rings: K_j is released when S_j completes, V_j only
-  // when PV_j does, one block later, so K gets the deeper ring.
-  static constexpr bool fits(int ks, int vs) { return 2 * Q_BYTES + (ks + vs) * KV_BYTES + BAR_BYTES <= kSmemLimitP; }
+  static constexpr int STATS_BYTES = 2 * 2 * BM * 4;  // [buffer][m, l][row] fp32
+  static constexpr bool fits(int ks, int vs) {
+    return 2 * Q_BYTES + (ks + vs) * KV_BYTES + BAR_BYTES + STATS_BYTES <= kSmemLimitP;
+  }
+  // K_j is released when S_j completes, V_j only when PV_j does: K gets the deeper ring.
   static constexpr int KS = fits(4, 4) || fits(4, 3) ? 4 : 3;
   static constexpr int VS = fits(4, 4) ? 4 : fits(4, 3) ? 3 : 2;
-  static constexpr int SMEM = 2 * Q_BYTES + (KS + VS) * KV_BYTES + BAR_BYTES;
+  static constexpr int SMEM = 2 * Q_BYTES + (KS + VS) * KV_BYTES + BAR_BYTES + STATS_BYTES;
   static constexpr int O_COL0 = 2 * BN;
   static constexpr int TMEM_COLS = 2 * BN + 2 * D <= 256 ? 256 : 512;
   static_assert(SMEM <= kSmemLimitP, "shared memory budget");
   static_assert(2 * BN + 2 * D <= 512, "TMEM budget");
-  static_assert((2 * KS + 2 * VS + 14) * 8 + 16 <= BAR_BYTES, "barrier area");
+  static_assert((2 * KS + 2 * VS + 18 + 2 * kTileRing) * 8 + 8 + 4 * kTileRing <= BAR_BYTES, "barrier area");
 };
 
 template <int D, int BN, bool BF16>
-__global__ void __launch_bounds__(192, 1)
+__global__ void __launch_bounds__(kThreadsP, 1)
     attn_tcp_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
-                    const __grid_constant__ CUtensorMap tmV, const __grid_constant__ CUtensorMap tmO,
-                    const TcpParams p) {
+                    const __grid_constant__ CUtensorMap tmV, const TcpParams p) {
   using C = TcpCfg<D, BN>;
   constexpr int KS = C::KS, VS = C::VS;
   extern __shared__ __align__(1024) uint8_t smem[];
@@ -86,28 +117,33 @@ __global__ void __launch_bounds__(192, 1)
     if (threadIdx.x == 0) set_err(p.err, BSA_DEVERR_ALIGN);
     return;
   }
-  uint8_t* sQ = smem;  // [2][Q_BYTES]
-  uint8_t* sK = sQ + 2 * C::Q_BYTES;  // [KS][KV_BYTES]
+  uint8_t* sQ = smem;                   // [2][Q_BYTES]
+  uint8_t* sK = sQ + 2 * C::Q_BYTES;    // [KS][KV_BYTES]
   uint8_t* sV = sK + KS * C::KV_BYTES;  // [VS][KV_BYTES]
   uint64_t* bars = reinterpret_cast<uint64_t*>(sV + VS * C::KV_BYTES);
-  uint64_t* q_full = bars;          // [2]
-  uint64_t* q_empty = q_full + 2;   // [2] epilogue's TMA store has read the buffer
-  uint64_t* k_full = q_empty + 2;   // [KS]
-  uint64_t* k_empty = k_full + KS;  // [KS] S MMA has read K
-  uint64_t* v_full = k_empty + KS;  // [VS]
-  uint64_t* v_empty = v_full + VS;  // [VS] PV MMA has read V
-  uint64_t* s_full = v_empty + VS;  // [2]
-  uint64_t* p_ready = s_full + 2;        // [2]
-  uint64_t* o_empty = p_ready + 2;       // [2] epilogue has read O buffer
-  uint64_t* pv_done = o_empty + 2;       // one phase per PV (rescale waits for PV_{j-1})
-  uint64_t* o_final = pv_done + 1;       // one phase per non-empty tile: its last PV completed
-  uint64_t* drain = o_final + 1;
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain + 1);
+  float* stats = reinterpret_cast<float*>(reinterpret_cast<uint8_t*>(bars) + C::BAR_BYTES);
+  uint64_t* q_full = bars;               // [2]
+  uint64_t* q_empty = q_full + 2;        // [2] the tile's last S has read Q
+  uint64_t* k_full = q_empty + 2;        // [KS]
+  uint64_t* k_empty = k_full + KS;       // [KS] S MMA has read K
+  uint64_t* v_full = k_empty + KS;       // [VS]
+  uint64_t* v_empty = v_full + VS;       // [VS] PV MMA has read V
+  uint64_t* s_full = v_empty + VS;       // [2] by S buffer
+  uint64_t* p_ready = s_full + 2;        // [2] by S buffer, 4 softmax warps
+  uint64_t* o_final = p_ready + 2;       // [2] by O buffer: the tile's last PV completed
+  uint64_t* o_empty = o_final + 2;       // [2] by O buffer: 4 epilogue warps read O
+  uint64_t* stats_ready = o_empty + 2;   // [2] 4 softmax warps wrote (m, l)
+  uint64_t* stats_empty = stats_ready + 2;  // [2] 4 epilogue warps read (m, l)
+  uint64_t* pv_done = stats_empty + 2;   // one phase per PV
+  uint64_t* drain = pv_done + 1;
+  uint64_t* tile_ready = drain + 1;              // [kTileRing] producer wrote the entry
+  uint64_t* tile_free = tile_ready + kTileRing;  // [kTileRing] all kTileUsers read it
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(tile_free + kTileRing);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+  volatile int* tile_ring = abort_flag + 1;      // [kTileRing] tile number, -1 = no more
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
-  const int G = gridDim.x;
 
   if (threadIdx.x == 0) {
     for (int i = 0; i < 2; ++i) {
@@ -115,7 +151,10 @@ __global__ void __launch_bounds__(192, 1)
       mbar_init(&q_empty[i], 1);
       mbar_init(&s_full[i], 1);
       mbar_init(&p_ready[i], 4);
+      mbar_init(&o_final[i], 1);
       mbar_init(&o_empty[i], 4);
+      mbar_init(&stats_ready[i], 4);
+      mbar_init(&stats_empty[i], 4);
     }
     for (int i = 0; i < KS; ++i) {
       mbar_init(&k_full[i], 1);
@@ -126,8 +165,11 @@ __global__ void __launch_bounds__(192, 1)
       mbar_init(&v_empty[i], 1);
     }
     mbar_init(pv_done, 1);
-    mbar_init(o_final, 1);
     mbar_init(drain, 1);
+    for (int i = 0; i < kTileRing; ++i) {
+      mbar_init(&tile_ready[i], 1);
+      mbar_init(&tile_free[i], kTileUsers);
+    }
     *abort_flag = 0;
     fence_mbar_init();
   }
@@ -140,26 +182,33 @@ __global__ void __launch_bounds__(192, 1)
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
 
-  // tile w -> (slice s, entries e0 .. e0+n, b, h, t)
+  // tile w -> (entries e0 .. e0+n of the plan, b, h, tile row t)
   auto tile_info = [&](int w, int& e0, int& n, int& b, int& h, int& t) {
     const int bh = w / p.T;
-    t = w - bh * p.T;
+    const int r = w - bh * p.T;
     b = bh / p.H;
     h = bh - b * p.H;
     const int s = (p.mask_b == 1 ? 0 : b) * p.mask_h + (p.mask_h == 1 ? 0 : h);
+    t = p.tile_order ? p.tile_order[s * p.T + r] : r;
     e0 = p.tile_ptr[s * p.T + t];
     n = p.tile_ptr[s * p.T + t + 1] - e0;
   };
+  // i-th tile of this CTA from the ring (all lanes of the calling warp, or one
+  // thread); -1 when there are no more or a wait failed
+  auto next_tile = [&](int i) -> int {
+    const int ri = i % kTileRing;
+    if (!mbar_wait(&tile_ready[ri], (i / kTileRing) & 1, abort_flag, p.err)) return -1;
+    return tile_ring[ri];
+  };
 
-  if (warp == 0) {
-    // ------------------------------------------------------------ producer
-    if (lane == 0) {
+  if (warp < 4) {
+    regs_dec<kRegsIssueP>();
+    if (warp == 0 && lane == 0) {
+      // ------------------------------------------------------------ producer
       tma_prefetch_desc(&tmQ);
       tma_prefetch_desc(&tmK);
       tma_prefetch_desc(&tmV);
-      // Loads in the order Q(tile), K_g, V_{g-1}: V runs one block behind K
-      // because PV_{g-1} is issued after S_g.
-      int e = 0, g = 0, gv = 0;  // non-empty tiles, K loads, V loads so far
+      int e = 0, g = 0, gv = 0;           // non-empty tiles, K loads, V loads so far
       int pv_b = 0, pv_h = 0, pv_kb = 0;  // the block whose V is still to load (gv < g)
       bool ok = true;
       auto load_v = [&]() -> bool {
@@ -171,7 +220,15 @@ __global__ void __launch_bounds__(192, 1)
         ++gv;
         return true;
       };
-      for (int w = blockIdx.x; ok && w < p.total_tiles; w += G) {
+      for (int i = 0; ok; ++i) {
+        // claim the next tile and pass its number on
+        const uint32_t claim = atomicAdd(&g_work_next[p.slot], 1u);
+        const int w = claim < static_cast<uint32_t>(p.total_tiles) ? static_cast<int>(claim) : -1;
+        const int ri = i % kTileRing;
+        if (i >= kTileRing && !(ok = mbar_wait(&tile_free[ri], ((i / kTileRing) - 1) & 1, abort_flag, p.err))) break;
+        tile_ring[ri] = w;
+        mbar_arrive(&tile_ready[ri]);
+        if (w < 0) break;
         int e0, n, b, h, t;
         tile_info(w, e0, n, b, h, t);
         if (n == 0) continue;
@@ -199,14 +256,12 @@ __global__ void __launch_bounds__(192, 1)
         }
       }
       if (ok && gv < g) ok = load_v();
-      if (*abort_flag) {
+      if (*abort_flag) {  // let the loads in flight land before the CTA exits
         for (int j = g > KS ? g - KS : 0; j < g; ++j) mbar_wait(&k_full[j % KS], (j / KS) & 1, nullptr, nullptr);
         for (int j = gv > VS ? gv - VS : 0; j < gv; ++j) mbar_wait(&v_full[j % VS], (j / VS) & 1, nullptr, nullptr);
       }
-    }
-  } else if (warp == 1) {
-    // ------------------------------------------------------------ MMA issuer
-    if (lane == 0) {
+    } else if (warp == 1 && lane == 0) {
+      // ------------------------------------------------------------ MMA issuer
       constexpr uint32_t idesc_qk = make_idesc_f16(BF16, 128, BN, false, false);
       constexpr uint32_t idesc_pv = make_idesc_f16(BF16, 128, D, false, true);
       const uint32_t q_addr = smem_u32(sQ);
@@ -214,7 +269,7 @@ __global__ void __launch_bounds__(192, 1)
       const uint32_t v_addr = smem_u32(sV);
       int e = 0;   // non-empty tiles so far
       int jg = 0;  // blocks (S MMAs) so far
-      // the PV still to issue: block index, its stage, O buffer, first / last block of its tile
+      // the PV still to issue: block index, O buffer, first / last block of its tile
       int pend_j = -1, pend_ob = 0;
       bool pend_first = false, pend_last = false;
       bool ok = true;
@@ -236,14 +291,17 @@ __global__ void __launch_bounds__(192, 1)
         }
         tc_commit(&v_empty[st]);
         tc_commit(pv_done);
-        if (pend_last) tc_commit(o_final);
+        if (pend_last) tc_commit(&o_final[pend_ob]);
         if (pend_first) ++pv_issued_tiles;
         pend_j = -1;
         return true;
       };
-      for (int w = blockIdx.x; ok && w < p.total_tiles; w += G) {
+      for (int i = 0; ok; ++i) {
+        const int w = next_tile(i);
+        if (w < 0) break;
         int e0, n, b, h, t;
         tile_info(w, e0, n, b, h, t);
+        mbar_arrive(&tile_free[i % kTileRing]);
         if (n == 0) continue;
         const int qb = e & 1;
         if (!(ok = mbar_wait(&q_full[qb], (e >> 1) & 1, abort_flag, p.err))) break;
@@ -262,6 +320,7 @@ __global__ void __launch_bounds__(192, 1)
           }
           tc_commit(&s_full[jg & 1]);
           tc_commit(&k_empty[st]);
+          if (j == n - 1) tc_commit(&q_empty[qb]);
           if (pend_j >= 0 && !(ok = do_pv())) break;
           pend_j = jg;
           pend_ob = e & 1;
@@ -274,39 +333,28 @@ __global__ void __launch_bounds__(192, 1)
       tc_commit(drain);
       mbar_wait(drain, 0, nullptr, nullptr);
     }
-  } else {
-    // ------------------------------------------------------------ softmax warpgroup + epilogue
-    const int q4 = warp & 3;
+  } else if (warp < 8) {
+    regs_inc<kRegsSoftmaxP>();
+    // -------------------------------------------------------------- softmax
+    const int q4 = warp & 3;  // TMEM lane quarter this warp may access
     const int row = q4 * 32 + lane;
     const uint32_t lane_base = tmem + (static_cast<uint32_t>(q4 * 32) << 16);
     const int half = row >> 6;
-    const bool store_thread = warp == 2 && lane == 0;
     int e = 0, jg = 0;
-    int pending_store_qb = -1;  // Q buffer whose TMA store still has to be waited for
     bool ok = true;
-    for (int w = blockIdx.x; w < p.total_tiles; w += G) {
+    for (int i = 0;; ++i) {
+      const int w = __shfl_sync(0xffffffffu, next_tile(i), 0);
+      if (w < 0) break;
       int e0, n, b, h, t;
       tile_info(w, e0, n, b, h, t);
-      const int grow0 = t * 128;
-      if (n == 0) {
-        // no kept block: O = 0 and lse = -inf for the tile's rows (plain stores)
-        const int grow = grow0 + row;
-        if (grow < p.N) {
-          const int64_t bh = static_cast<int64_t>(b) * p.H + h;
-          uint4* dst = reinterpret_cast<uint4*>(static_cast<uint8_t*>(p.o_raw) +
-                                                2 * (b * p.os_b + h * p.os_h + grow * p.os_n));
-#pragma unroll
-          for (int i = 0; i < D / 8; ++i) dst[i] = make_uint4(0, 0, 0, 0);
-          if (p.lse) p.lse[bh * p.N + grow] = -INFINITY;
-        }
-        continue;
-      }
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&tile_free[i % kTileRing]);
+      if (n == 0) continue;  // the epilogue writes its zero rows
       const int ob = e & 1;
       float m_run = -INFINITY, l_run = 0.f;
       for (int j = 0; j < n; ++j, ++jg) {
         const int sb = jg & 1;
-        // after a failed wait (ok false) every later wait returns at once (abort flag); the
-        // loops still run to keep all warps on the same named-barrier sequence
+        // after a failed wait every later wait returns at once (abort flag)
         if (!(ok = ok && __all_sync(0xffffffffu, mbar_wait(&s_full[sb], (jg >> 1) & 1, abort_flag, p.err))))
           continue;
         tc_fence_after();
@@ -315,11 +363,10 @@ __global__ void __launch_bounds__(192, 1)
         for (int c = 0; c < BN / 32; ++c) tmem_ld32(lane_base + sb * BN + c * 32, &sr[c * 32]);
         tmem_wait_ld();
         const uint32_t entry = static_cast<uint32_t>(__ldg(&p.tile_col[e0 + j]));
-        const uint32_t flags = entry >> 24;
-        const bool active = BN == 128 ? true : (((flags >> half) & 1u) != 0);
-        // keys at or past N (a partial last key block; TMA zero-filled them) are
-        // masked out: only the one block that crosses N takes this branch
+        const bool active = BN == 128 ? true : (((entry >> 24 >> half) & 1u) != 0);
         {
+          // keys at or past N (a partial last key block; TMA zero-filled them) are
+          // masked out: only the one block that crosses N takes this branch
           const int kvalid = p.N - static_cast<int>(entry & 0xFFFFFFu) * BN;
           if (kvalid < BN) {
 #pragma unroll
@@ -355,57 +402,83 @@ __global__ void __launch_bounds__(192, 1)
         tc_fence_before();
         __syncwarp();
         if (lane == 0) mbar_arrive(&p_ready[sb]);
-        if (j == 0 && store_thread && pending_store_qb >= 0) {
-          // the previous tile's output store must have read its Q buffer
-          tma_store_wait_read0();
-          mbar_arrive(&q_empty[pending_store_qb]);
-          pending_store_qb = -1;
-        }
       }
-      // ---------------------------------------------------------- epilogue of this tile
-      ok = ok && __all_sync(0xffffffffu, mbar_wait(o_final, e & 1, abort_flag, p.err));
-      if (ok) {
-      tc_fence_after();
-      uint32_t o_all[D];
-#pragma unroll
-      for (int c = 0; c < D / 32; ++c) tmem_ld32(lane_base + C::O_COL0 + ob * D + c * 32, &o_all[c * 32]);
-      tmem_wait_ld();
-      tc_fence_before();
+      // hand the row's (m, l) to the epilogue warps
+      if (e >= 2)
+        ok = ok && __all_sync(0xffffffffu, mbar_wait(&stats_empty[ob], ((e >> 1) - 1) & 1, abort_flag, p.err));
+      stats[ob * 256 + row] = m_run;
+      stats[ob * 256 + 128 + row] = l_run;
       __syncwarp();
-      if (lane == 0) mbar_arrive(&o_empty[ob]);  // the MMA may start the tile after next in this buffer
-      const float inv_l = l_run > 0.f ? 1.f / l_run : 0.f;
-      uint8_t* orow = sQ + (e & 1) * C::Q_BYTES + row * 128;  // this tile's Q buffer: no MMA reads it any more
+      if (lane == 0) mbar_arrive(&stats_ready[ob]);
+      ++e;
+    }
+  } else {
+    regs_dec<kRegsEpilogueP>();
+    // ------------------------------------------------------------- epilogue
+    const int q4 = warp & 3;
+    const int row = q4 * 32 + lane;
+    const uint32_t lane_base = tmem + (static_cast<uint32_t>(q4 * 32) << 16);
+    int e = 0;
+    bool ok = true;
+    for (int i = 0;; ++i) {
+      const int w = __shfl_sync(0xffffffffu, next_tile(i), 0);
+      if (w < 0) break;
+      int e0, n, b, h, t;
+      tile_info(w, e0, n, b, h, t);
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&tile_free[i % kTileRing]);
+      const int grow = t * 128 + row;
+      uint8_t* orow = p.o + 2 * (b * p.os_b + h * p.os_h + static_cast<int64_t>(grow) * p.os_n);
+      float* lrow = p.lse ? p.lse + (static_cast<int64_t>(b) * p.H + h) * p.N + grow : nullptr;
+      if (n == 0) {
+        // no kept block: O = 0 and lse = -inf for the tile's rows
+        if (grow < p.N) {
 #pragma unroll
-      for (int c = 0; c < D / 32; ++c) {
-        uint8_t* chunk_row = orow + (c >> 1) * C::Q_CHUNK;
-#pragma unroll
-        for (int g2 = 0; g2 < 4; ++g2) {
-          const uint32_t* o = &o_all[c * 32 + 8 * g2];
-          uint4 v;
-          v.x = pack2<BF16>(__uint_as_float(o[0]) * inv_l, __uint_as_float(o[1]) * inv_l);
-          v.y = pack2<BF16>(__uint_as_float(o[2]) * inv_l, __uint_as_float(o[3]) * inv_l);
-          v.z = pack2<BF16>(__uint_as_float(o[4]) * inv_l, __uint_as_float(o[5]) * inv_l);
-          v.w = pack2<BF16>(__uint_as_float(o[6]) * inv_l, __uint_as_float(o[7]) * inv_l);
-          const int gran = ((c & 1) * 4 + g2) ^ (row & 7);  // 128-byte swizzle
-          *reinterpret_cast<uint4*>(chunk_row + gran * 16) = v;
+          for (int i = 0; i < D / 8; ++i) reinterpret_cast<uint4*>(orow)[i] = make_uint4(0, 0, 0, 0);
+          if (lrow) *lrow = -INFINITY;
         }
+        continue;
       }
-      fence_proxy_async_smem();
-      const int grow = grow0 + row;
-      if (p.lse && grow < p.N)
-        p.lse[(static_cast<int64_t>(b) * p.H + h) * p.N + grow] = l_run > 0.f ? m_run + log2f(l_run) : -INFINITY;
+      const int ob = e & 1;
+      ok = ok && __all_sync(0xffffffffu, mbar_wait(&stats_ready[ob], (e >> 1) & 1, abort_flag, p.err));
+      float m_run = 0.f, l_run = 0.f;
+      if (ok) {
+        m_run = stats[ob * 256 + row];
+        l_run = stats[ob * 256 + 128 + row];
       }
-      named_bar_sync(1, 128);  // every softmax warp, once per non-empty tile, also after a failure
-      if (store_thread && !*abort_flag) {
-        // (the previous tile's buffer was released at this tile's block 0)
-        for (int c = 0; c < C::NCHUNK; ++c)
-          tma_store_4d(&tmO, sQ + (e & 1) * C::Q_BYTES + c * C::Q_CHUNK, c * 64, grow0, h, b);
-        tma_store_commit();
-        pending_store_qb = e & 1;
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&stats_empty[ob]);
+      ok = ok && __all_sync(0xffffffffu, mbar_wait(&o_final[ob], (e >> 1) & 1, abort_flag, p.err));
+      if (ok) {
+        tc_fence_after();
+        const float inv_l = l_run > 0.f ? 1.f / l_run : 0.f;
+#pragma unroll
+        for (int c = 0; c < D / 32; ++c) {
+          uint32_t o[32];
+          tmem_ld32(lane_base + C::O_COL0 + ob * D + c * 32, o);
+          tmem_wait_ld();
+          if (c == D / 32 - 1) {
+            // every read of O_e is done: the MMA may start tile e+2 in this buffer
+            tc_fence_before();
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&o_empty[ob]);
+          }
+          if (grow < p.N) {
+#pragma unroll
+            for (int g = 0; g < 4; ++g) {
+              uint4 v;
+              v.x = pack2<BF16>(__uint_as_float(o[8 * g + 0]) * inv_l, __uint_as_float(o[8 * g + 1]) * inv_l);
+              v.y = pack2<BF16>(__uint_as_float(o[8 * g + 2]) * inv_l, __uint_as_float(o[8 * g + 3]) * inv_l);
+              v.z = pack2<BF16>(__uint_as_float(o[8 * g + 4]) * inv_l, __uint_as_float(o[8 * g + 5]) * inv_l);
+              v.w = pack2<BF16>(__uint_as_float(o[8 * g + 6]) * inv_l, __uint_as_float(o[8 * g + 7]) * inv_l);
+              reinterpret_cast<uint4*>(orow)[c * 4 + g] = v;
+            }
+          }
+        }
+        if (lrow && grow < p.N) *lrow = l_run > 0.f ? m_run + log2f(l_run) : -INFINITY;
       }
       ++e;
     }
-    if (store_thread) tma_store_wait0();
   }
 
   tc_fence_before();
@@ -413,6 +486,15 @@ __global__ void __launch_bounds__(192, 1)
   if (warp == 1) {
     tc_fence_after();
     tmem_dealloc(tmem, C::TMEM_COLS);
+  }
+  if (threadIdx.x == 0) {
+    // every claim of this CTA is done; the last CTA resets the slot for the next launch
+    __threadfence();
+    if (atomicAdd(&g_work_done[p.slot], 1u) == gridDim.x - 1) {
+      g_work_next[p.slot] = 0;
+      g_work_done[p.slot] = 0;
+      __threadfence();
+    }
   }
 }
 
@@ -430,17 +512,27 @@ int sm_count() {
 template <int D, int BN, bool BF16>
 int launch_p(const bsa_fwd_args* a, cudaStream_t st) {
   using C = TcpCfg<D, BN>;
-  CUtensorMap mq, mk, mv, mo;
+  auto kern = attn_tcp_kernel<D, BN, BF16>;
+  // The setmaxnreg split needs the launch to hold at least the sum of the
+  // three warpgroups' shares; with fewer the increase would never be granted.
+  static int checked = 0;  // 1 ok, 2 too few registers
+  if (!checked) {
+    cudaFuncAttributes fa;
+    BSA_CUDA_CHECK(cudaFuncGetAttributes(&fa, kern));
+    checked = fa.numRegs * kThreadsP >= 128 * (kRegsIssueP + kRegsSoftmaxP + kRegsEpilogueP) ? 1 : 2;
+  }
+  if (checked != 1) return BSA_ERR_UNSUPPORTED;
+  CUtensorMap mq, mk, mv;
   int r;
   if ((r = make_tensor_map_4d(&mq, a->q, a->B, a->H, a->N, D, BF16, 128))) return r;
   if ((r = make_tensor_map_4d(&mk, a->k, a->B, a->H, a->N, D, BF16, BN))) return r;
   if ((r = make_tensor_map_4d(&mv, a->v, a->B, a->H, a->N, D, BF16, BN))) return r;
-  if ((r = make_tensor_map_4d(&mo, a->o, a->B, a->H, a->N, D, BF16, 128))) return r;
   TcpParams p;
   p.tile_ptr = a->plan.tile_ptr;
   p.tile_col = a->plan.tile_col;
+  p.tile_order = a->plan.tile_order;
   p.lse = a->lse;
-  p.o_raw = a->o.data;
+  p.o = static_cast<uint8_t*>(a->o.data);
   p.os_b = a->o.stride_b;
   p.os_h = a->o.stride_h;
   p.os_n = a->o.stride_n;
@@ -453,15 +545,12 @@ int launch_p(const bsa_fwd_args* a, cudaStream_t st) {
   p.mask_h = a->plan.mask_h;
   p.total_tiles = a->B * a->H * p.T;
   p.scale_log2 = a->sm_scale * 1.4426950408889634f;
-  auto kern = attn_tcp_kernel<D, BN, BF16>;
+  static std::atomic<unsigned> launches{0};
+  p.slot = static_cast<int>(launches.fetch_add(1, std::memory_order_relaxed) % kWorkSlots);
   BSA_CUDA_CHECK(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM));
-  int per_sm = 1;
-  BSA_CUDA_CHECK(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kern, 192, C::SMEM));
-  if (per_sm < 1) per_sm = 1;
-  if (C::TMEM_COLS * per_sm > 512) per_sm = 512 / C::TMEM_COLS;
-  int grid = sm_count() * per_sm;
+  int grid = sm_count();
   if (grid > p.total_tiles) grid = p.total_tiles;
-  kern<<<grid, 192, C::SMEM, st>>>(mq, mk, mv, mo, p);
+  kern<<<grid, kThreadsP, C::SMEM, st>>>(mq, mk, mv, p);
   return cudaGetLastError() == cudaSuccess ? BSA_OK : BSA_ERR_CUDA;
 }
 

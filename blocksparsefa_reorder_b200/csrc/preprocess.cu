@@ -118,6 +118,33 @@ __device__ __forceinline__ int64_t load_index(const void* p, int dtype, int64_t 
 
 // Copy rows of `VB`-byte vectors, one vector per thread.  Rows are (b, h, i)
 // with i in [0, N); the permutation is the same for every (b, h).
+// Work order of a plan: the rank of tile row t among its slice's rows by
+// (decreasing kept-block count, increasing row), stored as
+// order[s*T + rank] = t.  One thread per row; the slice's counts are streamed
+// through shared memory 256 at a time.  Ranks are distinct, so the result is
+// a permutation of 0..T-1 per slice and deterministic.
+__global__ void __launch_bounds__(256) tile_order_kernel(const int32_t* __restrict__ tile_ptr, int T,
+                                                         int32_t* __restrict__ order) {
+  __shared__ int cnt[256];
+  const int64_t base_s = static_cast<int64_t>(blockIdx.y) * T;
+  const int t = blockIdx.x * 256 + threadIdx.x;
+  const int32_t* ptr = tile_ptr + base_s;
+  const int mine = t < T ? ptr[t + 1] - ptr[t] : 0;
+  int rank = 0;
+  for (int base = 0; base < T; base += 256) {
+    const int u = base + threadIdx.x;
+    cnt[threadIdx.x] = u < T ? ptr[u + 1] - ptr[u] : 0;
+    __syncthreads();
+    const int lim = T - base < 256 ? T - base : 256;
+    for (int i = 0; i < lim; ++i) {
+      const int c = cnt[i];
+      rank += (c > mine) || (c == mine && base + i < t);
+    }
+    __syncthreads();
+  }
+  if (t < T) order[base_s + rank] = t;
+}
+
 template <int VB>
 __global__ void permute_rows_kernel(uint8_t* __restrict__ dst, const uint8_t* __restrict__ src, int64_t dsb,
                                     int64_t dsh, int64_t dsn, int64_t ssb, int64_t ssh, int64_t ssn, int H, int N,
@@ -310,6 +337,19 @@ extern "C" int bsa_build_plan(const uint8_t* mask, int64_t stride_b, int64_t str
   r = launch_plan_scan(counts, ptr_len - 1, tile_ptr, st);
   if (r) return r;
   return launch_plan_fill(mask, stride_b, stride_h, stride_row, mask_b, mask_h, nb, block, tile_ptr, tile_col, st);
+}
+
+extern "C" int bsa_build_tile_order(const int32_t* tile_ptr, int32_t mask_b, int32_t mask_h, int32_t nb,
+                                    int32_t block, int32_t* tile_order, void* stream) {
+  const int rc = bsa_plan_sizes(mask_b, mask_h, nb, block, nullptr, nullptr, nullptr);
+  if (rc != BSA_OK) return rc;
+  if (!tile_ptr || !tile_order) return BSA_ERR_INVALID_ARG;
+  const int64_t T = tiles_per_row(nb, block);
+  const int64_t slices = static_cast<int64_t>(mask_b) * mask_h;
+  if (slices > 65535) return BSA_ERR_UNSUPPORTED;  // grid.y
+  const dim3 grid(static_cast<unsigned>((T + 255) / 256), static_cast<unsigned>(slices));
+  tile_order_kernel<<<grid, 256, 0, static_cast<cudaStream_t>(stream)>>>(tile_ptr, static_cast<int>(T), tile_order);
+  return cudaGetLastError() == cudaSuccess ? BSA_OK : BSA_ERR_CUDA;
 }
 
 extern "C" int bsa_permute_rows(bsa_tensor4d dst, bsa_tensor4d src, int32_t B, int32_t H, int32_t N, int32_t D,

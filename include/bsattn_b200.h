@@ -33,7 +33,7 @@ extern "C" {
 #define BSA_API
 #endif
 
-#define BSA_ABI_VERSION 1
+#define BSA_ABI_VERSION 2
 
 typedef enum bsa_status {
   BSA_OK = 0,
@@ -75,13 +75,17 @@ typedef struct bsa_tensor4d {
  * (mask_h==1 ? 0 : h) are tile_ptr[s*T + t] .. tile_ptr[s*T + t + 1] in
  * tile_col, T = ceil(nb * BLOCK / 128).  Each entry is (flags << 24) |
  * key_block, ascending in key_block; flags bit 0 / bit 1 = the first /
- * second block row of the tile keeps that key block. */
+ * second block row of the tile keeps that key block.
+ * tile_order (optional, output of bsa_build_tile_order, NULL = natural
+ * order): for each slice, its T tile rows by decreasing number of kept
+ * blocks; the tcgen05 kernel hands tiles to CTAs in that order. */
 typedef struct bsa_plan {
   const int32_t* tile_ptr;
   const int32_t* tile_col;
   int32_t mask_b, mask_h;
   int32_t nb;    /* ceil(N / block) */
   int32_t block; /* 64 or 128 */
+  const int32_t* tile_order;
 } bsa_plan;
 
 typedef struct bsa_fwd_args {
@@ -114,6 +118,17 @@ BSA_API int bsa_plan_sizes(int32_t mask_b, int32_t mask_h, int32_t nb, int32_t b
 BSA_API int bsa_build_plan(const uint8_t* mask, int64_t stride_b, int64_t stride_h, int64_t stride_row,
                            int32_t mask_b, int32_t mask_h, int32_t nb, int32_t block, int32_t* tile_ptr,
                            int32_t* tile_col, void* workspace, size_t workspace_bytes, void* stream);
+
+/* Work order for a built plan: tile_order[s*T + r] = the tile row with the
+ * r-th largest kept-block count in slice s (ties by increasing row), for the
+ * mask_b*mask_h slices (tile_order holds tile_ptr_len - 1 entries).  With it
+ * the tcgen05 kernel's CTAs claim tiles dynamically, longest first, which
+ * balances their load.  No counterpart in the reference, whose grid is one
+ * static program per query block (BlockSparseTriton_Naive.py:56-57,
+ * triton_kernels/BlockSparse_Naive.py:80-81).  Needs no workspace; enqueued on
+ * `stream`. */
+BSA_API int bsa_build_tile_order(const int32_t* tile_ptr, int32_t mask_b, int32_t mask_h, int32_t nb, int32_t block,
+                                 int32_t* tile_order, void* stream);
 
 /* bsa_build_plan for callers that may not allocate device memory (a host
  * framework that owns every device buffer through its own pool, a serving

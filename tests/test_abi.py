@@ -87,6 +87,8 @@ def test_other_entry_points_validate_on_host():
     assert L.bsa_inverse_permutation(None, 1, 0, None, None, None) == 0               # empty: nothing to do
     assert L.bsa_inverse_permutation(0x1000, 5, 4, 0x2000, None, None) == 3
     assert L.bsa_remap_indices(None, -1, None, 0, None, None, None) == 1
+    assert L.bsa_build_tile_order(None, 1, 1, 4, 128, 0x1000, None) == 1               # no tile_ptr
+    assert L.bsa_build_tile_order(0x1000, 1, 1, 4, 96, 0x2000, None) == 5              # block size
     assert L.bsa_blockmask_from_coords(None, None, 0, 0, 64, 1, 1, None, None, None, None, None) == 1
     size = ctypes.c_size_t()
     assert L.bsa_fwd_reordered_workspace_bytes(ctypes.byref(_args()), ctypes.byref(size)) == 0

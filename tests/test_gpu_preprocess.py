@@ -27,6 +27,23 @@ def test_plan_build_bitexact(dev, block, nb, shape, p):
     assert np.array_equal(plan.tile_col[:n].cpu().numpy(), col)
 
 
+@pytest.mark.parametrize("block,nb,shape,p", [(128, 64, (1, 1), 0.1), (64, 33, (2, 3), 0.3), (64, 8, (1, 2), 0.0),
+                                             (128, 700, (1, 2), 0.02), (64, 600, (1, 1), 0.5)])
+def test_tile_order(dev, block, nb, shape, p):
+    """The plan's work order: per slice, the tile rows by decreasing number of
+    kept blocks, ties by increasing row (a stable descending sort), including
+    slices with more than one 256-row chunk."""
+    rng = np.random.default_rng(nb + 1)
+    m = rng.random(shape + (nb, nb)) < p
+    m[..., : nb // 3, :] = False  # some empty rows
+    plan = BlockSparsePlan(torch.from_numpy(m).to(dev), block)
+    T = plan.tiles_per_row
+    n = np.diff(plan.tile_ptr.cpu().numpy()).reshape(-1, T)
+    want = np.argsort(-n, axis=1, kind="stable")
+    got = plan.tile_order.cpu().numpy().reshape(-1, T)
+    assert np.array_equal(got, want)
+
+
 def test_plan_from_strided_mask(dev):
     rng = np.random.default_rng(5)
     big = torch.from_numpy(rng.random((2, 3, 16, 20)) < 0.4).to(dev)
