@@ -53,7 +53,7 @@ def load_peaks():
 def profile_traffic(name: str):
     """DRAM bytes per launch of the attention kernel from the committed ncu
     summary (its ``dram_bytes_per_launch_full: <number>`` line)."""
-    p = ROOT / "profiles" / f"attn_tc_{name}.md"
+    p = ROOT / "profiles" / f"attn_tcp_{name}.md"
     if not p.exists():
         return None
     m = re.search(r"dram_bytes_per_launch_full:\s*([0-9.eE+]+)", p.read_text())
@@ -240,7 +240,8 @@ def run_ours(args):
     kp = torch.from_numpy(wl.kv_perm).to(dev) if wl.kv_perm is not None else None
     o = torch.empty_like(q)
     stream = torch.cuda.current_stream(dev)
-    launches_per_step = 3 + 1 + (4 if qp is not None else 0)
+    # plan build (count, scan, fill, work order) + the attention kernel (+ the permutation passes)
+    launches_per_step = 4 + 1 + (4 if qp is not None else 0)
     k_events = []
 
     def step(record=False):
@@ -327,7 +328,7 @@ def run_ours(args):
                          (4 * q.numel() * q.element_size() // 2**20)},
         "roofline": {"bound": "tensor", "achieved": achieved, "peak": peak, "unit": "TFLOP/s",
                      "frac": achieved / peak, "traffic": profile_traffic(wl.name),
-                     "kernel": "attn_tc_kernel", "kernel_ms": kern_ms,
+                     "kernel": "attn_tcp_kernel", "kernel_ms": kern_ms,
                      "peak_source": f"bf16_tflops (burst) of {peak_kind} peaks"},
         "e2e": {"value": wl.flops * world / (e2e_ms * 1e-3) / 1e12, "unit": UNIT, "ms_per_step": e2e_ms,
                 "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,

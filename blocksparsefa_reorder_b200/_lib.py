@@ -60,7 +60,7 @@ PROTOS = {
     "bsa_device_supported": ([ctypes.c_int, ctypes.POINTER(ctypes.c_int)], ctypes.c_int),
     "bsa_plan_sizes": ([_i32, _i32, _i32, _i32, ctypes.POINTER(_i64), ctypes.POINTER(_i64), ctypes.POINTER(_sz)],
                        ctypes.c_int),
-    "bsa_build_plan": ([_vp, _i64, _i64, _i64, _i32, _i32, _i32, _i32, _vp, _vp, _vp, _sz, _vp], ctypes.c_int),
+    "bsa_build_plan": ([_vp, _i64, _i64, _i64, _i32, _i32, _i32, _i32, _vp, _vp, _vp, _vp, _sz, _vp], ctypes.c_int),
     "bsa_build_plan_noalloc": ([_vp, _i64, _i64, _i64, _i32, _i32, _i32, _i32, _vp, _vp, _vp], ctypes.c_int),
     "bsa_build_tile_order": ([_vp, _i32, _i32, _i32, _i32, _vp, _vp], ctypes.c_int),
     "bsa_fwd": ([ctypes.POINTER(FwdArgs), _vp], ctypes.c_int),

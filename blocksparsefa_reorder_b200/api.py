@@ -82,7 +82,8 @@ class BlockSparsePlan:
     every mask byte (``BlockSparse_Naive.py:25-32``) and can be reused across
     calls with the same mask.  It also holds the work order the tcgen05
     kernel hands tiles out in (each slice's tiles by decreasing kept-block
-    count).  Building it enqueues four small kernels and does not synchronise.
+    count).  Building it enqueues one kernel for small masks (four for large
+    ones) and does not synchronise.
     """
 
     def __init__(self, block_mask: torch.Tensor, block: int):
@@ -108,12 +109,11 @@ class BlockSparsePlan:
         self.tile_ptr = torch.empty(ptr_len.value, dtype=torch.int32, device=self.device)
         self.tile_col = torch.empty(max(1, cap.value), dtype=torch.int32, device=self.device)
         work = torch.empty(max(1, (ws.value + 3) // 4), dtype=torch.int32, device=self.device)
+        self.tile_order = torch.empty(max(1, ptr_len.value - 1), dtype=torch.int32, device=self.device)
         _lib.check(L.bsa_build_plan(m.data_ptr(), m.stride(0), m.stride(1), m.stride(2), self.mask_b, self.mask_h,
                                     self.nb, self.block, self.tile_ptr.data_ptr(), self.tile_col.data_ptr(),
-                                    work.data_ptr(), ws.value, _stream(self.device)), "bsa_build_plan")
-        self.tile_order = torch.empty(max(1, ptr_len.value - 1), dtype=torch.int32, device=self.device)
-        _lib.check(L.bsa_build_tile_order(self.tile_ptr.data_ptr(), self.mask_b, self.mask_h, self.nb, self.block,
-                                          self.tile_order.data_ptr(), _stream(self.device)), "bsa_build_tile_order")
+                                    self.tile_order.data_ptr(), work.data_ptr(), ws.value, _stream(self.device)),
+                   "bsa_build_plan")
         self._mask_ref = m  # keep the mask alive until the kernels ran
         self._work = work
 

@@ -111,6 +111,118 @@ __global__ void __launch_bounds__(1024) plan_scan_kernel(const int32_t* __restri
   if (tid == blockDim.x - 1) tile_ptr[n] = run;
 }
 
+// Whole plan (and optionally its work order) in one CTA for small masks,
+// where the multi-kernel path is all launch latency: the mask is staged in
+// shared memory by all threads at once (independent loads), then per-tile
+// counts, a block-wide exclusive scan into tile_ptr, the fill of tile_col and
+// each tile's rank in its slice.  n = slices * T <= kSmallPlanTiles and the
+// mask is at most kSmallPlanMaskBytes.
+constexpr int kSmallPlanTiles = 4096;
+constexpr int kSmallPlanSliceTiles = 1024;
+constexpr int kSmallPlanMaskBytes = 96 * 1024;
+
+__global__ void __launch_bounds__(1024) plan_small_kernel(const uint8_t* __restrict__ mask, int64_t sb, int64_t sh,
+                                                          int64_t srow, int mask_h, int nb, int rows_per_tile, int T,
+                                                          int n, bool vec16, int32_t* __restrict__ tile_ptr,
+                                                          int32_t* __restrict__ tile_col,
+                                                          int32_t* __restrict__ tile_order) {
+  __shared__ int32_t cnt[kSmallPlanTiles];
+  __shared__ int32_t off[kSmallPlanTiles + 1];
+  __shared__ int32_t warp_sums[32];
+  extern __shared__ uint8_t smask[];  // [slices][nb][nb]
+  const int tid = threadIdx.x, lane = tid & 31, wid = tid >> 5;
+  const uint32_t lt_mask = (1u << lane) - 1u;
+  const int slices = n / T;
+  const int nn = nb * nb;  // <= kSmallPlanMaskBytes
+  const int rows = slices * nb;
+  if (vec16) {
+    // 16-byte vectors: every load of the CTA is independent and coalesced
+    const int vpr = nb / 16;
+    for (int i = tid; i < rows * vpr; i += 1024) {
+      const int rr = i / vpr, v = i - rr * vpr;
+      const int s = rr / nb, r = rr - s * nb;
+      const uint8_t* src = mask + static_cast<int64_t>(s / mask_h) * sb + static_cast<int64_t>(s % mask_h) * sh +
+                           r * srow + v * 16;
+      *reinterpret_cast<uint4*>(smask + rr * nb + v * 16) = *reinterpret_cast<const uint4*>(src);
+    }
+  } else {
+    for (int i = tid; i < rows * nb; i += 1024) {
+      const int rr = i / nb, c = i - rr * nb;
+      const int s = rr / nb, r = rr - s * nb;
+      smask[i] = mask[static_cast<int64_t>(s / mask_h) * sb + static_cast<int64_t>(s % mask_h) * sh + r * srow + c];
+    }
+  }
+  __syncthreads();
+  // counts, one warp per tile
+  for (int w = wid; w < n; w += 32) {
+    const int s = w / T, t = w - (w / T) * T;
+    const uint8_t* base = smask + s * nn;
+    int count = 0;
+    for (int j0 = 0; j0 < nb; j0 += 32) {
+      const uint32_t f = tile_flags(base, nb, nb, rows_per_tile, t, j0 + lane);
+      count += __popc(__ballot_sync(0xffffffffu, f != 0));
+    }
+    if (lane == 0) cnt[w] = count;
+  }
+  __syncthreads();
+  // exclusive scan: each thread a contiguous chunk, then warp and block totals
+  const int chunk = (n + 1023) / 1024;
+  const int lo = tid * chunk < n ? tid * chunk : n;
+  const int hi = lo + chunk < n ? lo + chunk : n;
+  int32_t local = 0;
+  for (int i = lo; i < hi; ++i) local += cnt[i];
+  int32_t x = local;
+  for (int o = 1; o < 32; o <<= 1) {
+    const int32_t y = __shfl_up_sync(0xffffffffu, x, o);
+    if (lane >= o) x += y;
+  }
+  if (lane == 31) warp_sums[wid] = x;
+  __syncthreads();
+  if (wid == 0) {
+    int32_t ws = warp_sums[lane];
+    for (int o = 1; o < 32; o <<= 1) {
+      const int32_t y = __shfl_up_sync(0xffffffffu, ws, o);
+      if (lane >= o) ws += y;
+    }
+    warp_sums[lane] = ws;
+  }
+  __syncthreads();
+  int32_t run = x - local + (wid > 0 ? warp_sums[wid - 1] : 0);
+  for (int i = lo; i < hi; ++i) {
+    off[i] = run;
+    run += cnt[i];
+  }
+  if (tid == 1023) off[n] = run;
+  __syncthreads();
+  for (int i = tid; i <= n; i += 1024) tile_ptr[i] = off[i];
+  // fill, one warp per tile
+  for (int w = wid; w < n; w += 32) {
+    const int s = w / T, t = w - (w / T) * T;
+    const uint8_t* base = smask + s * nn;
+    int pos = off[w];
+    for (int j0 = 0; j0 < nb; j0 += 32) {
+      const int j = j0 + lane;
+      const uint32_t f = tile_flags(base, nb, nb, rows_per_tile, t, j);
+      const uint32_t bal = __ballot_sync(0xffffffffu, f != 0);
+      if (f) tile_col[pos + __popc(bal & lt_mask)] = static_cast<int32_t>((f << 24) | static_cast<uint32_t>(j));
+      pos += __popc(bal);
+    }
+  }
+  // work order: rank by (decreasing count, increasing row) within the slice
+  if (tile_order) {
+    for (int w = tid; w < n; w += 1024) {
+      const int s0 = (w / T) * T, t = w - s0;
+      const int mine = cnt[w];
+      int rank = 0;
+      for (int u = 0; u < T; ++u) {
+        const int c = cnt[s0 + u];
+        rank += (c > mine) || (c == mine && u < t);
+      }
+      tile_order[s0 + rank] = t;
+    }
+  }
+}
+
 __device__ __forceinline__ int64_t load_index(const void* p, int dtype, int64_t i) {
   return dtype == BSA_INDEX_I64 ? static_cast<const int64_t*>(p)[i]
                                 : static_cast<int64_t>(static_cast<const int32_t*>(p)[i]);
@@ -322,7 +434,8 @@ extern "C" int bsa_plan_sizes(int32_t mask_b, int32_t mask_h, int32_t nb, int32_
 
 extern "C" int bsa_build_plan(const uint8_t* mask, int64_t stride_b, int64_t stride_h, int64_t stride_row,
                               int32_t mask_b, int32_t mask_h, int32_t nb, int32_t block, int32_t* tile_ptr,
-                              int32_t* tile_col, void* workspace, size_t workspace_bytes, void* stream) {
+                              int32_t* tile_col, int32_t* tile_order, void* workspace, size_t workspace_bytes,
+                              void* stream) {
   size_t need = 0;
   int64_t ptr_len = 0, cap = 0;
   const int rc = bsa_plan_sizes(mask_b, mask_h, nb, block, &ptr_len, &cap, &need);
@@ -331,12 +444,33 @@ extern "C" int bsa_build_plan(const uint8_t* mask, int64_t stride_b, int64_t str
   if (!workspace || workspace_bytes < need) return BSA_ERR_WORKSPACE;
   if (cap > INT32_MAX) return BSA_ERR_UNSUPPORTED;
   cudaStream_t st = static_cast<cudaStream_t>(stream);
+  const int T = tiles_per_row(nb, block);
+  const int64_t n = ptr_len - 1;
+  const int64_t mask_bytes = static_cast<int64_t>(mask_b) * mask_h * nb * nb;
+  if (n <= kSmallPlanTiles && T <= kSmallPlanSliceTiles && mask_bytes <= kSmallPlanMaskBytes) {
+    static bool attr_set[64];
+    int dev = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return BSA_ERR_CUDA;
+    if (!attr_set[dev]) {
+      BSA_CUDA_CHECK(
+          cudaFuncSetAttribute(plan_small_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmallPlanMaskBytes));
+      attr_set[dev] = true;
+    }
+    const bool vec16 = reinterpret_cast<uintptr_t>(mask) % 16 == 0 && nb % 16 == 0 && stride_row % 16 == 0 &&
+                       (mask_b == 1 || stride_b % 16 == 0) && (mask_h == 1 || stride_h % 16 == 0);
+    plan_small_kernel<<<1, 1024, static_cast<size_t>(mask_bytes), st>>>(
+        mask, stride_b, stride_h, stride_row, mask_h, nb, 128 / block, T, static_cast<int>(n), vec16, tile_ptr,
+        tile_col, tile_order);
+    return cudaGetLastError() == cudaSuccess ? BSA_OK : BSA_ERR_CUDA;
+  }
   int32_t* counts = static_cast<int32_t*>(workspace);
   int r = launch_plan_count(mask, stride_b, stride_h, stride_row, mask_b, mask_h, nb, block, counts, st);
   if (r) return r;
-  r = launch_plan_scan(counts, ptr_len - 1, tile_ptr, st);
+  r = launch_plan_scan(counts, n, tile_ptr, st);
   if (r) return r;
-  return launch_plan_fill(mask, stride_b, stride_h, stride_row, mask_b, mask_h, nb, block, tile_ptr, tile_col, st);
+  r = launch_plan_fill(mask, stride_b, stride_h, stride_row, mask_b, mask_h, nb, block, tile_ptr, tile_col, st);
+  if (r || !tile_order) return r;
+  return bsa_build_tile_order(tile_ptr, mask_b, mask_h, nb, block, tile_order, stream);
 }
 
 extern "C" int bsa_build_tile_order(const int32_t* tile_ptr, int32_t mask_b, int32_t mask_h, int32_t nb,

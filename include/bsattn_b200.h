@@ -114,10 +114,14 @@ BSA_API int bsa_plan_sizes(int32_t mask_b, int32_t mask_h, int32_t nb, int32_t b
 /* Block mask (bytes, nonzero = kept, [mask_b, mask_h, nb, nb] with the given
  * element strides) -> per-tile CSR.  Replaces the per-query-block scan of
  * every mask byte inside the reference kernel
- * (triton_kernels/BlockSparse_Naive.py:25-32, BlockSparse_Fused.py:29-35). */
+ * (triton_kernels/BlockSparse_Naive.py:25-32, BlockSparse_Fused.py:29-35).
+ * tile_order (optional, tile_ptr_len - 1 entries) also receives the plan's
+ * work order (see bsa_build_tile_order).  Small plans (<= 4096 tiles, <= 1024
+ * per slice) are built by a single one-CTA kernel. */
 BSA_API int bsa_build_plan(const uint8_t* mask, int64_t stride_b, int64_t stride_h, int64_t stride_row,
                            int32_t mask_b, int32_t mask_h, int32_t nb, int32_t block, int32_t* tile_ptr,
-                           int32_t* tile_col, void* workspace, size_t workspace_bytes, void* stream);
+                           int32_t* tile_col, int32_t* tile_order, void* workspace, size_t workspace_bytes,
+                           void* stream);
 
 /* Work order for a built plan: tile_order[s*T + r] = the tile row with the
  * r-th largest kept-block count in slice s (ties by increasing row), for the

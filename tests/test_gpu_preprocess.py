@@ -15,8 +15,11 @@ from oracle import preprocess as OP
 pytestmark = pytest.mark.gpu
 
 
+# the last two cases exceed the one-kernel plan build (T > 1024 tiles per
+# slice; > 4096 tiles in all) and take the multi-kernel path
 @pytest.mark.parametrize("block,nb,shape,p", [(128, 64, (1, 1), 0.1), (64, 33, (2, 3), 0.3), (64, 8, (1, 2), 0.0),
-                                             (128, 5, (2, 1), 1.0), (64, 512, (1, 1), 0.05)])
+                                             (128, 5, (2, 1), 1.0), (64, 512, (1, 1), 0.05),
+                                             (128, 1100, (1, 1), 0.01), (64, 40, (16, 16), 0.2)])
 def test_plan_build_bitexact(dev, block, nb, shape, p):
     rng = np.random.default_rng(nb)
     m = rng.random(shape + (nb, nb)) < p
@@ -28,7 +31,8 @@ def test_plan_build_bitexact(dev, block, nb, shape, p):
 
 
 @pytest.mark.parametrize("block,nb,shape,p", [(128, 64, (1, 1), 0.1), (64, 33, (2, 3), 0.3), (64, 8, (1, 2), 0.0),
-                                             (128, 700, (1, 2), 0.02), (64, 600, (1, 1), 0.5)])
+                                             (128, 700, (1, 2), 0.02), (64, 600, (1, 1), 0.5),
+                                             (128, 1100, (1, 1), 0.01), (64, 40, (16, 16), 0.2)])
 def test_tile_order(dev, block, nb, shape, p):
     """The plan's work order: per slice, the tile rows by decreasing number of
     kept blocks, ties by increasing row (a stable descending sort), including

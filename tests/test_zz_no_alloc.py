@@ -38,7 +38,8 @@ def _plan_with_workspace(L, m, block, stream):
     tc = torch.full((cap.value,), -1, dtype=torch.int32, device=m.device)
     work = torch.empty(max(1, ws.value // 4), dtype=torch.int32, device=m.device)
     _lib.check(L.bsa_build_plan(m.data_ptr(), m.stride(0), m.stride(1), m.stride(2), mb, mh, nb, block,
-                                tp.data_ptr(), tc.data_ptr(), work.data_ptr(), ws.value, stream), "bsa_build_plan")
+                                tp.data_ptr(), tc.data_ptr(), None, work.data_ptr(), ws.value, stream),
+               "bsa_build_plan")
     return tp, tc
 
 
