@@ -240,8 +240,14 @@ def run_ours(args):
     kp = torch.from_numpy(wl.kv_perm).to(dev) if wl.kv_perm is not None else None
     o = torch.empty_like(q)
     stream = torch.cuda.current_stream(dev)
-    # plan build (count, scan, fill, work order) + the attention kernel (+ the permutation passes)
-    launches_per_step = 4 + 1 + (4 if qp is not None else 0)
+    # plan build: one kernel for small masks (<= 4096 tiles, <= 1024 per slice, <= 96 KiB of mask), else
+    # count, scan, fill and work order; K and V permutation passes when kv_perm is given (the query
+    # permutation is applied inside the attention kernel); the attention kernel
+    ms = mask.shape
+    slices, nb = (ms[0] * ms[1], ms[-1]) if mask.dim() == 4 else (1, ms[-1])
+    tiles_per_slice = (nb * wl.block + 127) // 128
+    small = slices * tiles_per_slice <= 4096 and tiles_per_slice <= 1024 and slices * nb * nb <= 96 * 1024
+    launches_per_step = (1 if small else 4) + (2 if kp is not None else 0) + 1
     k_events = []
 
     def step(record=False):

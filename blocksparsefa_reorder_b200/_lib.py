@@ -22,7 +22,7 @@ STATUS_NAMES = {
 DTYPE_F32, DTYPE_F16, DTYPE_BF16 = 0, 1, 2
 INDEX_I32, INDEX_I64 = 0, 1
 KERNEL_AUTO, KERNEL_SIMT, KERNEL_TCGEN05 = 0, 1, 2
-DEVERR_TIMEOUT, DEVERR_PERM_RANGE, DEVERR_PERM_DUP, DEVERR_COORD, DEVERR_PLAN = 1, 2, 4, 8, 16
+DEVERR_TIMEOUT, DEVERR_PERM_RANGE, DEVERR_PERM_DUP, DEVERR_COORD, DEVERR_PLAN, DEVERR_ALIGN = 1, 2, 4, 8, 16, 32
 ABI_VERSION = 2
 PLAN_NOALLOC_MAX_TILES = 1 << 20
 

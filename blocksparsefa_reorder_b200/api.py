@@ -139,7 +139,8 @@ def _check_err(err: Optional[torch.Tensor], what: str) -> None:
                  (_lib.DEVERR_PERM_RANGE, "permutation value out of range"),
                  (_lib.DEVERR_PERM_DUP, "permutation value repeated"),
                  (_lib.DEVERR_COORD, "coordinate out of range"),
-                 (_lib.DEVERR_PLAN, "plan entry out of range")]
+                 (_lib.DEVERR_PLAN, "plan entry out of range"),
+                 (_lib.DEVERR_ALIGN, "dynamic shared memory misaligned")]
         bits = [n for b, n in names if v & b]
         status = _lib.STATUS_NAMES[7] if v & _lib.DEVERR_TIMEOUT else _lib.STATUS_NAMES[6]
         raise RuntimeError(f"{what}: device check failed ({status}): {', '.join(bits)}")

@@ -52,8 +52,14 @@ size_t round256(size_t x) { return (x + 255) & ~size_t(255); }
 // CTA form.
 int launch_tc(const bsa_fwd_args* a, cudaStream_t st) { return launch_attn_tcp(a, st); }
 
+// The fused reordered forward: the tcgen05 kernel gathers Q rows and
+// scatters O / lse rows through q_perm itself; only K and V are permuted
+// beforehand.
+bool fused_reorder(const bsa_fwd_args* a) { return a->kernel != BSA_KERNEL_SIMT && attn_tc_supported(a); }
+
 // Workspace layout of bsa_fwd_reordered, 256-byte aligned regions:
-//   [q'] [k' v'] [o' lse'] -- q', o', lse' when q_perm is given, k', v' when kv_perm is.
+//   [q'] [k' v'] [o' lse'] -- k', v' when kv_perm is given; q', o', lse' when
+//   q_perm is and the forward is not the fused one.
 struct ReorderLayout {
   size_t q, k, v, o, lse, total;
 };
@@ -147,7 +153,7 @@ extern "C" int bsa_fwd_reordered_workspace_bytes(const bsa_fwd_args* a, size_t* 
   if (!a || !bytes) return BSA_ERR_INVALID_ARG;
   const int rc = validate_fwd(a);
   if (rc) return rc;
-  *bytes = reorder_layout(a, true, true).total;
+  *bytes = reorder_layout(a, !fused_reorder(a), true).total;
   return BSA_OK;
 }
 
@@ -156,13 +162,27 @@ extern "C" int bsa_fwd_reordered(const bsa_fwd_args* a, const void* q_perm, cons
   int rc = validate_fwd(a);
   if (rc) return rc;
   if ((q_perm || kv_perm) && perm_dtype != BSA_INDEX_I32 && perm_dtype != BSA_INDEX_I64) return BSA_ERR_DTYPE;
-  const ReorderLayout L = reorder_layout(a, q_perm != nullptr, kv_perm != nullptr);
+  const bool fused = fused_reorder(a);
+  const ReorderLayout L = reorder_layout(a, !fused && q_perm != nullptr, kv_perm != nullptr);
   if (L.total && (!workspace || workspace_bytes < L.total)) return BSA_ERR_WORKSPACE;
   if ((rc = check_device())) return rc;
   cudaStream_t st = static_cast<cudaStream_t>(stream);
   uint8_t* ws = static_cast<uint8_t*>(workspace);
   const int eb = dtype_bytes(a->dtype);
   bsa_fwd_args inner = *a;
+  if (fused) {
+    if (kv_perm) {
+      inner.k = contiguous(ws + L.k, a);
+      inner.v = contiguous(ws + L.v, a);
+      if ((rc = launch_permute_rows(inner.k, a->k, a->B, a->H, a->N, a->D, eb, kv_perm, perm_dtype, 0, a->err_flag,
+                                    st)))
+        return rc;
+      if ((rc = launch_permute_rows(inner.v, a->v, a->B, a->H, a->N, a->D, eb, kv_perm, perm_dtype, 0, a->err_flag,
+                                    st)))
+        return rc;
+    }
+    return launch_attn_tcp(&inner, st, q_perm, perm_dtype);
+  }
   if (q_perm) {
     inner.q = contiguous(ws + L.q, a);
     if ((rc = launch_permute_rows(inner.q, a->q, a->B, a->H, a->N, a->D, eb, q_perm, perm_dtype, 0, a->err_flag, st)))

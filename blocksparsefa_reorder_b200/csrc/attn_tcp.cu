@@ -20,7 +20,12 @@
 //  * warpgroup 1: softmax, one query row per thread, P written back into
 //    the first BN/2 columns of S's TMEM;
 //  * warpgroup 2: epilogue, one query row per thread: O / l from TMEM
-//    straight to global memory, lse, and the zero rows of empty tiles.
+//    straight to global memory, lse, and the zero rows of empty tiles;
+//  * warps 2-3, with a query permutation only: gather the tile's Q rows
+//    q[q_perm[row]] into the Q buffer (the layout the TMA load would give).
+// With a query permutation (the fused variant, BlockSparse_Fused.py:173-223)
+// Q rows are read from q_perm[row] and O / lse rows written to q_perm[row];
+// the mask is in the permuted order.
 // The epilogue has its own warps so that the softmax goes straight on to the
 // next tile while the previous tile's output is written.
 //
@@ -57,7 +62,7 @@ __device__ uint32_t g_work_next[kWorkSlots];
 __device__ uint32_t g_work_done[kWorkSlots];
 
 constexpr int kTileRing = 8;   // tile numbers in flight between the producer and the other roles
-constexpr int kTileUsers = 9;  // MMA thread + 4 softmax warps + 4 epilogue warps
+constexpr int kTileUsers = 11;  // MMA thread + 4 softmax + 4 epilogue + 2 Q-gather warps
 
 struct TcpParams {
   const int32_t* tile_ptr;
@@ -67,6 +72,10 @@ struct TcpParams {
   uint8_t* o;                // output base (16-bit elements)
   int64_t os_b, os_h, os_n;  // output strides in elements
   int32_t* err;
+  const uint8_t* q;           // query base, for the gather of permuted rows
+  int64_t qs_b, qs_h, qs_n;   // query strides in elements
+  const void* q_perm;         // optional query permutation (new row -> old row)
+  int perm_dtype;             // bsa_index_dtype of q_perm
   int H, N, nb, T, mask_b, mask_h, total_tiles;
   int slot;  // work counter slot
   float scale_log2;
@@ -81,6 +90,11 @@ constexpr int kRegsIssueP = 72;
 constexpr int kRegsSoftmaxP = 240;
 constexpr int kRegsEpilogueP = 96;
 static_assert(128 * (kRegsIssueP + kRegsSoftmaxP + kRegsEpilogueP) <= kThreadsP * kRegsLaunchP, "register split");
+
+__device__ __forceinline__ int64_t load_perm(const void* perm, int dtype, int64_t i) {
+  return dtype == BSA_INDEX_I64 ? __ldg(static_cast<const int64_t*>(perm) + i)
+                                : static_cast<int64_t>(__ldg(static_cast<const int32_t*>(perm) + i));
+}
 
 template <int D, int BN>
 struct TcpCfg {
@@ -147,7 +161,7 @@ __global__ void __launch_bounds__(kThreadsP, 1)
 
   if (threadIdx.x == 0) {
     for (int i = 0; i < 2; ++i) {
-      mbar_init(&q_full[i], 1);
+      mbar_init(&q_full[i], p.q_perm ? 2 : 1);  // gather warps, or the TMA transaction
       mbar_init(&q_empty[i], 1);
       mbar_init(&s_full[i], 1);
       mbar_init(&p_ready[i], 4);
@@ -233,10 +247,12 @@ __global__ void __launch_bounds__(kThreadsP, 1)
         tile_info(w, e0, n, b, h, t);
         if (n == 0) continue;
         const int qb = e & 1;
-        if (e >= 2 && !(ok = mbar_wait(&q_empty[qb], ((e >> 1) - 1) & 1, abort_flag, p.err))) break;
-        mbar_arrive_expect_tx(&q_full[qb], C::Q_BYTES);
-        for (int c = 0; c < C::NCHUNK; ++c)
-          tma_load_4d(sQ + qb * C::Q_BYTES + c * C::Q_CHUNK, &tmQ, &q_full[qb], c * 64, t * 128, h, b);
+        if (!p.q_perm) {  // (permuted queries: warps 2-3 gather Q)
+          if (e >= 2 && !(ok = mbar_wait(&q_empty[qb], ((e >> 1) - 1) & 1, abort_flag, p.err))) break;
+          mbar_arrive_expect_tx(&q_full[qb], C::Q_BYTES);
+          for (int c = 0; c < C::NCHUNK; ++c)
+            tma_load_4d(sQ + qb * C::Q_BYTES + c * C::Q_CHUNK, &tmQ, &q_full[qb], c * 64, t * 128, h, b);
+        }
         ++e;
         for (int j = 0; j < n; ++j, ++g) {
           const int st = g % KS;
@@ -332,6 +348,51 @@ __global__ void __launch_bounds__(kThreadsP, 1)
       if (ok && pend_j >= 0) ok = do_pv();
       tc_commit(drain);
       mbar_wait(drain, 0, nullptr, nullptr);
+    } else if (warp >= 2) {
+      // ------------------------------------------------- Q gather (permuted queries)
+      // Warp 2 fills rows 0-63 of the tile, warp 3 rows 64-127, each row
+      // as 16-byte granules into the 128-byte-swizzled chunks the MMA reads.
+      const int gw = warp - 2;
+      int e = 0;
+      bool ok = true;
+      for (int i = 0;; ++i) {
+        const int w = __shfl_sync(0xffffffffu, next_tile(i), 0);
+        if (w < 0) break;
+        int e0, n, b, h, t;
+        tile_info(w, e0, n, b, h, t);
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&tile_free[i % kTileRing]);
+        if (!p.q_perm || n == 0) continue;
+        const int qb = e & 1;
+        if (e >= 2)
+          ok = ok && __all_sync(0xffffffffu, mbar_wait(&q_empty[qb], ((e >> 1) - 1) & 1, abort_flag, p.err));
+        ++e;
+        if (!ok) continue;
+        for (int k = 0; k < 2; ++k) {
+          const int r = gw * 64 + k * 32 + lane;
+          const int grow = t * 128 + r;
+          const uint4* src = nullptr;
+          if (grow < p.N) {
+            const int64_t old = load_perm(p.q_perm, p.perm_dtype, grow);
+            if (old >= 0 && old < p.N)
+              src = reinterpret_cast<const uint4*>(p.q + 2 * (b * p.qs_b + h * p.qs_h + old * p.qs_n));
+            else
+              set_err(p.err, BSA_DEVERR_PERM_RANGE);
+          }
+#pragma unroll
+          for (int c = 0; c < C::NCHUNK; ++c) {
+            uint8_t* dst = sQ + qb * C::Q_BYTES + c * C::Q_CHUNK + r * 128;
+            uint4 v[8];
+#pragma unroll
+            for (int g = 0; g < 8; ++g) v[g] = src ? __ldg(src + c * 8 + g) : make_uint4(0, 0, 0, 0);
+#pragma unroll
+            for (int g = 0; g < 8; ++g) *reinterpret_cast<uint4*>(dst + ((g ^ (r & 7)) * 16)) = v[g];
+          }
+        }
+        fence_proxy_async_smem();  // generic-proxy writes, read by the tensor cores
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&q_full[qb]);
+      }
     }
   } else if (warp < 8) {
     regs_inc<kRegsSoftmaxP>();
@@ -428,11 +489,21 @@ __global__ void __launch_bounds__(kThreadsP, 1)
       __syncwarp();
       if (lane == 0) mbar_arrive(&tile_free[i % kTileRing]);
       const int grow = t * 128 + row;
-      uint8_t* orow = p.o + 2 * (b * p.os_b + h * p.os_h + static_cast<int64_t>(grow) * p.os_n);
-      float* lrow = p.lse ? p.lse + (static_cast<int64_t>(b) * p.H + h) * p.N + grow : nullptr;
+      // destination row: the permuted query's original row
+      int64_t drow = grow;
+      if (p.q_perm && grow < p.N) {
+        drow = load_perm(p.q_perm, p.perm_dtype, grow);
+        if (drow < 0 || drow >= p.N) {
+          set_err(p.err, BSA_DEVERR_PERM_RANGE);
+          drow = p.N;  // no store
+        }
+      }
+      const bool store = grow < p.N && drow < p.N;
+      uint8_t* orow = p.o + 2 * (b * p.os_b + h * p.os_h + drow * p.os_n);
+      float* lrow = p.lse ? p.lse + (static_cast<int64_t>(b) * p.H + h) * p.N + drow : nullptr;
       if (n == 0) {
         // no kept block: O = 0 and lse = -inf for the tile's rows
-        if (grow < p.N) {
+        if (store) {
 #pragma unroll
           for (int i = 0; i < D / 8; ++i) reinterpret_cast<uint4*>(orow)[i] = make_uint4(0, 0, 0, 0);
           if (lrow) *lrow = -INFINITY;
@@ -463,7 +534,7 @@ __global__ void __launch_bounds__(kThreadsP, 1)
             __syncwarp();
             if (lane == 0) mbar_arrive(&o_empty[ob]);
           }
-          if (grow < p.N) {
+          if (store) {
 #pragma unroll
             for (int g = 0; g < 4; ++g) {
               uint4 v;
@@ -475,7 +546,7 @@ __global__ void __launch_bounds__(kThreadsP, 1)
             }
           }
         }
-        if (lrow && grow < p.N) *lrow = l_run > 0.f ? m_run + log2f(l_run) : -INFINITY;
+        if (lrow && store) *lrow = l_run > 0.f ? m_run + log2f(l_run) : -INFINITY;
       }
       ++e;
     }
@@ -510,7 +581,7 @@ int sm_count() {
 }
 
 template <int D, int BN, bool BF16>
-int launch_p(const bsa_fwd_args* a, cudaStream_t st) {
+int launch_p(const bsa_fwd_args* a, cudaStream_t st, const void* q_perm, int perm_dtype) {
   using C = TcpCfg<D, BN>;
   auto kern = attn_tcp_kernel<D, BN, BF16>;
   // The setmaxnreg split needs the launch to hold at least the sum of the
@@ -531,6 +602,12 @@ int launch_p(const bsa_fwd_args* a, cudaStream_t st) {
   p.tile_ptr = a->plan.tile_ptr;
   p.tile_col = a->plan.tile_col;
   p.tile_order = a->plan.tile_order;
+  p.q = static_cast<const uint8_t*>(a->q.data);
+  p.qs_b = a->q.stride_b;
+  p.qs_h = a->q.stride_h;
+  p.qs_n = a->q.stride_n;
+  p.q_perm = q_perm;
+  p.perm_dtype = perm_dtype;
   p.lse = a->lse;
   p.o = static_cast<uint8_t*>(a->o.data);
   p.os_b = a->o.stride_b;
@@ -556,11 +633,13 @@ int launch_p(const bsa_fwd_args* a, cudaStream_t st) {
 
 }  // namespace
 
-int launch_attn_tcp(const bsa_fwd_args* a, cudaStream_t st) {
+int launch_attn_tcp(const bsa_fwd_args* a, cudaStream_t st, const void* q_perm, int perm_dtype) {
   const bool bf16 = a->dtype == BSA_DTYPE_BF16;
   const int bn = a->plan.block;
-#define BSA_TCP_CASE(D_, BN_) \
-  if (a->D == D_ && bn == BN_) return bf16 ? launch_p<D_, BN_, true>(a, st) : launch_p<D_, BN_, false>(a, st);
+#define BSA_TCP_CASE(D_, BN_)                                                          \
+  if (a->D == D_ && bn == BN_)                                                         \
+    return bf16 ? launch_p<D_, BN_, true>(a, st, q_perm, perm_dtype) \
+                : launch_p<D_, BN_, false>(a, st, q_perm, perm_dtype);
   BSA_TCP_CASE(64, 64)
   BSA_TCP_CASE(64, 128)
   BSA_TCP_CASE(128, 64)

@@ -36,7 +36,10 @@ int launch_attn_tc(const bsa_fwd_args* a, cudaStream_t st);
 int make_tensor_map_4d(CUtensorMap* m, const bsa_tensor4d& t, int B, int H, int N, int D, bool bf16, int rows);
 
 // attn_tcp.cu: the same pipeline, persistent over tiles
-int launch_attn_tcp(const bsa_fwd_args* a, cudaStream_t st);
+// q_perm (optional, bsa_index_dtype perm_dtype): gather Q rows from and
+// scatter O / lse rows to q_perm[row] inside the kernel.
+int launch_attn_tcp(const bsa_fwd_args* a, cudaStream_t st, const void* q_perm = nullptr,
+                    int perm_dtype = BSA_INDEX_I64);
 
 
 }  // namespace bsa

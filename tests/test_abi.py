@@ -92,8 +92,12 @@ def test_other_entry_points_validate_on_host():
     assert L.bsa_blockmask_from_coords(None, None, 0, 0, 64, 1, 1, None, None, None, None, None) == 1
     size = ctypes.c_size_t()
     assert L.bsa_fwd_reordered_workspace_bytes(ctypes.byref(_args()), ctypes.byref(size)) == 0
-    # q', k', v', o' of 1*2*256*64 bf16 each (lse not requested)
+    # fused tcgen05 forward: k', v' of 1*2*256*64 bf16 each (Q and O go through the permutation in-kernel)
+    assert size.value == 2 * 2 * 256 * 64 * 2
+    assert L.bsa_fwd_reordered_workspace_bytes(ctypes.byref(_args(kernel=1)), ctypes.byref(size)) == 0
+    # SIMT forward: q', k', v', o' (lse not requested)
     assert size.value == 4 * 2 * 256 * 64 * 2
     a = _args()
-    assert L.bsa_fwd_reordered(ctypes.byref(a), 0x1000, None, 1, None, 0, None) == 9   # workspace missing
+    assert L.bsa_fwd_reordered(ctypes.byref(a), None, 0x1000, 1, None, 0, None) == 9   # workspace missing
+    assert L.bsa_fwd_reordered(ctypes.byref(_args(kernel=1)), 0x1000, None, 1, None, 0, None) == 9
     assert L.bsa_fwd_reordered(ctypes.byref(a), 0x1000, None, 7, 0x1000, 1 << 30, None) == 3  # perm dtype

@@ -118,6 +118,48 @@ def test_permuted_path_matches_oracle(dev, dtype):
     assert np.abs(lse.cpu().numpy() - ref_lse).max() <= TOL_LSE
 
 
+@pytest.mark.parametrize("which", ["q", "kv", "both"])
+@pytest.mark.parametrize("D,block,N,idx", [(128, 128, 1024, torch.int64), (64, 64, 64 * 13, torch.int32),
+                                           (128, 64, 64 * 9, torch.int64)])
+def test_fused_permutation(dev, which, D, block, N, idx):
+    """The reordered forward on the tcgen05 path gathers Q rows and scatters
+    O / lse rows through q_perm inside the attention kernel (K and V are
+    permuted beforehand): every combination of permutations, BLOCK 64 with a
+    partial last 128-row tile, int32 and int64 permutations, NaN-prefilled
+    outputs, against the oracle's reordered attention (BlockSparse_Fused.py
+    semantics: mask in the new order, output in the original order)."""
+    B, H = 2, 2
+    nb = (N + block - 1) // block
+    mask = _rand_mask(nb, 0.35, seed=D + N, shape=(1, H), empty_rows=(1,))
+    q, k, v = _qkv(B, H, N, D, torch.bfloat16, seed=N, dev=dev)
+    g = torch.Generator().manual_seed(N + D)
+    qp = torch.randperm(N, generator=g).to(idx).to(dev) if which in ("q", "both") else None
+    kp = torch.randperm(N, generator=g).to(idx).to(dev) if which in ("kv", "both") else None
+    o = torch.full_like(q, float("nan"))
+    lse = torch.full((B, H, N), float("nan"), device=dev)
+    o, lse = block_sparse_attention(q, k, v, torch.from_numpy(mask).to(dev), q_perm=qp, kv_perm=kp, return_lse=True,
+                                    out=o, lse_out=lse, kernel="tcgen05", check_errors=True)
+    ref, ref_lse = _oracle(q, k, v, mask, block, qp, kp)
+    assert _maxerr(o, ref) <= TOL_16
+    lv = lse.cpu().numpy()
+    fin = np.isfinite(ref_lse)
+    assert np.array_equal(np.isfinite(lv), fin)
+    assert np.abs(lv[fin] - ref_lse[fin]).max() <= TOL_LSE
+
+
+def test_fused_permutation_out_of_range_flagged(dev):
+    """A query permutation value outside [0, N) is reported through the error
+    word (the row is not read or written), not read out of bounds."""
+    B, H, N, D, block = 1, 1, 512, 128, 128
+    mask = _rand_mask(N // block, 0.5, seed=1)
+    q, k, v = _qkv(B, H, N, D, torch.bfloat16, seed=2, dev=dev)
+    qp = torch.arange(N, device=dev)
+    qp[7] = N + 5
+    with pytest.raises(RuntimeError, match="permutation value out of range"):
+        block_sparse_attention(q, k, v, torch.from_numpy(mask).to(dev), q_perm=qp, kernel="tcgen05",
+                               check_errors=True)
+
+
 def test_golden_reference_kernels(dev, golden_dir):
     """Our kernels against the reference Triton kernels' outputs, through the
     kernel-level drop-ins called like the reference runners call Triton."""
