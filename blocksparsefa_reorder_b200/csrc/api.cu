@@ -47,9 +47,6 @@ bool simt_supported(const bsa_fwd_args* a) { return a->D == 16 || a->D == 32 || 
 
 size_t round256(size_t x) { return (x + 255) & ~size_t(255); }
 
-// The persistent kernel (one CTA per SM looping over tiles) overlaps one
-// tile's epilogue with the next tile's start; attn_tc.cu is its one-tile-per-
-// CTA form.
 int launch_tc(const bsa_fwd_args* a, cudaStream_t st) { return launch_attn_tcp(a, st); }
 
 // The fused reordered forward: the tcgen05 kernel gathers Q rows and

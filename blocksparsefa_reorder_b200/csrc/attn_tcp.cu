@@ -195,6 +195,10 @@ __global__ void __launch_bounds__(kThreadsP, 1)
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
+  // Launched as a programmatic dependent of the plan build (or whatever ran
+  // before on the stream): everything above touched only this CTA's shared
+  // memory and TMEM; from here on global memory is read and written.
+  grid_dependency_wait();
 
   // tile w -> (entries e0 .. e0+n of the plan, b, h, tile row t)
   auto tile_info = [&](int w, int& e0, int& n, int& b, int& h, int& t) {
@@ -627,8 +631,21 @@ int launch_p(const bsa_fwd_args* a, cudaStream_t st, const void* q_perm, int per
   BSA_CUDA_CHECK(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM));
   int grid = sm_count();
   if (grid > p.total_tiles) grid = p.total_tiles;
-  kern<<<grid, kThreadsP, C::SMEM, st>>>(mq, mk, mv, p);
-  return cudaGetLastError() == cudaSuccess ? BSA_OK : BSA_ERR_CUDA;
+  // programmatic stream serialization: the CTAs may start (barriers, TMEM)
+  // while the previous kernel on the stream finishes; they wait for it in
+  // grid_dependency_wait() before touching global memory
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(grid);
+  cfg.blockDim = dim3(kThreadsP);
+  cfg.dynamicSmemBytes = C::SMEM;
+  cfg.stream = st;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  BSA_CUDA_CHECK(cudaLaunchKernelEx(&cfg, kern, mq, mk, mv, p));
+  return BSA_OK;
 }
 
 }  // namespace

@@ -29,13 +29,13 @@ int launch_permute_rows(bsa_tensor4d dst, bsa_tensor4d src, int B, int H, int N,
 // attn_simt.cu
 int launch_attn_simt(const bsa_fwd_args* a, cudaStream_t st);
 
-// attn_tc.cu
+// tma_maps.cu: whether the tcgen05 path takes these arguments (bf16 / fp16,
+// D 64 or 128, BLOCK 64 or 128, 16-byte-aligned rows), and the 4-D TMA map
+// over a [B, H, N, D] 16-bit tensor, box 64 x rows, 128-byte swizzle.
 bool attn_tc_supported(const bsa_fwd_args* a);
-int launch_attn_tc(const bsa_fwd_args* a, cudaStream_t st);
-// 4-D TMA map over a [B, H, N, D] 16-bit tensor, box 64 x rows, 128-byte swizzle.
 int make_tensor_map_4d(CUtensorMap* m, const bsa_tensor4d& t, int B, int H, int N, int D, bool bf16, int rows);
 
-// attn_tcp.cu: the same pipeline, persistent over tiles
+// attn_tcp.cu: the persistent tcgen05 attention forward
 // q_perm (optional, bsa_index_dtype perm_dtype): gather Q rows from and
 // scatter O / lse rows to q_perm[row] inside the kernel.
 int launch_attn_tcp(const bsa_fwd_args* a, cudaStream_t st, const void* q_perm = nullptr,

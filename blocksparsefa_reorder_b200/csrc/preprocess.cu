@@ -130,6 +130,9 @@ __global__ void __launch_bounds__(1024) plan_small_kernel(const uint8_t* __restr
   __shared__ int32_t off[kSmallPlanTiles + 1];
   __shared__ int32_t warp_sums[32];
   extern __shared__ uint8_t smask[];  // [slices][nb][nb]
+  // the attention kernel that follows may start its set-up on the other SMs;
+  // it waits for this kernel's completion before reading the plan
+  allow_dependents();
   const int tid = threadIdx.x, lane = tid & 31, wid = tid >> 5;
   const uint32_t lt_mask = (1u << lane) - 1u;
   const int slices = n / T;
