@@ -144,3 +144,25 @@ def test_head_sharding_reassembles_full_output(dev):
                                             v[:, h0:h1].contiguous(), mask))
     assert torch.equal(torch.cat(parts, dim=1), full)
     assert math.isfinite(full.float().abs().max().item())
+
+
+def test_cli_end_to_end(dev, tmp_path, capsys):
+    """The main.py-compatible command line on a small pattern file with row
+    and column permutation files (1-based, as the reference's files are):
+    prints the mask's NNZ line and the runner's two timing lines."""
+    from blocksparsefa_reorder_b200 import __main__ as cli
+
+    n = 512
+    rng = np.random.default_rng(3)
+    pairs = {(i, i) for i in range(n)} | {tuple(x) for x in rng.integers(0, n, size=(2000, 2))}
+    rows = np.array(sorted(pairs))
+    mtx = tmp_path / "pattern.mtx"
+    mtx.write_text(f"{n} {n} {len(rows)}\n" + "".join(f"{r + 1} {c + 1}\n" for r, c in rows))
+    for name, seed in (("rows.txt", 1), ("cols.txt", 2)):
+        perm = np.random.default_rng(seed).permutation(n) + 1
+        (tmp_path / name).write_text(f"{n}\n" + "".join(f"{v}\n" for v in perm))
+    assert cli.main([str(mtx), "--block-size", "64", "--head-dim", "64", "--row-reorder", str(tmp_path / "rows.txt"),
+                     "--col-reorder", str(tmp_path / "cols.txt")]) == 0
+    out = capsys.readouterr().out
+    assert "NNZ blocks:" in out
+    assert "Average time with reordering:" in out and "Average time without reordering:" in out

@@ -109,3 +109,22 @@ def test_build_script_lists_every_source():
     on_disk = sorted(p.name for p in build.CSRC.glob("*.cu"))
     assert sorted(build.SOURCES) == on_disk
     assert Path(build.LIB_PATH).name == "libbsattn_b200.so"
+
+
+def test_cli_arguments_follow_main_py(tmp_path):
+    """``python -m blocksparsefa_reorder_b200`` parses main.py's arguments
+    (main.py:102-160): defaults, the .mtx extension check, and the
+    reference's comparator modes reported as not included."""
+    from blocksparsefa_reorder_b200 import __main__ as cli
+
+    a = cli.parse_args([str(tmp_path / "p.mtx")])
+    assert (a.block_size, a.head_dim, a.num_heads, a.mode) == (128, 128, 1, "B200")
+    assert a.row_reorder is None and a.col_reorder is None
+    a = cli.parse_args([str(tmp_path / "p.MTX"), "--block-size", "64", "--head-dim", "64", "--num-heads", "4",
+                        "--row-reorder", "r.txt", "--col-reorder", "c.txt"])
+    assert (a.block_size, a.head_dim, a.num_heads) == (64, 64, 4)
+    assert str(a.row_reorder) == "r.txt" and str(a.col_reorder) == "c.txt"
+    for bad in (["p.txt"], ["p.mtx", "--mode", "BSFA"], ["p.mtx", "--block-size", "96"],
+                ["p.mtx", "--head-dim", "0"], ["p.mtx", "--mode", "XYZ"]):
+        with pytest.raises(SystemExit):
+            cli.parse_args(bad)
