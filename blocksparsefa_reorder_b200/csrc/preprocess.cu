@@ -113,31 +113,55 @@ __global__ void __launch_bounds__(1024) plan_scan_kernel(const int32_t* __restri
 
 // Whole plan (and optionally its work order) in one CTA for small masks,
 // where the multi-kernel path is all launch latency: the mask is staged in
-// shared memory by all threads at once (independent loads), then per-tile
-// counts, a block-wide exclusive scan into tile_ptr, the fill of tile_col and
-// each tile's rank in its slice.  n = slices * T <= kSmallPlanTiles and the
-// mask is at most kSmallPlanMaskBytes.
+// shared memory by all threads at once (independent loads); one thread per
+// (tile, 16-column chunk) turns its chunk into kept-column bit masks and
+// counts them; a block-wide exclusive scan of the tile counts gives
+// tile_ptr; each chunk thread then writes its entries at the tile's offset
+// plus the counts of the tile's earlier chunks; the tile ranks of the work
+// order are computed by groups of threads.  Limits: n = slices * T tiles <=
+// kSmallPlanTiles, n * chunks <= kSmallPlanChunks, mask <= kSmallPlanMaskBytes.
 constexpr int kSmallPlanTiles = 4096;
 constexpr int kSmallPlanSliceTiles = 1024;
 constexpr int kSmallPlanMaskBytes = 96 * 1024;
+constexpr int kSmallPlanChunks = 8192;
+
+// bit k = byte k of p[0, jmax) is nonzero; `aligned`: p is 16-byte aligned and jmax == 16
+__device__ __forceinline__ uint32_t nonzero_bits16(const uint8_t* p, int jmax, bool aligned) {
+  uint32_t m = 0;
+  if (aligned) {
+    const uint4 v = *reinterpret_cast<const uint4*>(p);
+    const uint32_t w[4] = {v.x, v.y, v.z, v.w};
+#pragma unroll
+    for (int k = 0; k < 4; ++k)
+#pragma unroll
+      for (int b = 0; b < 4; ++b) m |= (((w[k] >> (8 * b)) & 0xFFu) != 0u ? 1u : 0u) << (4 * k + b);
+  } else {
+    for (int k = 0; k < jmax; ++k) m |= (p[k] != 0 ? 1u : 0u) << k;
+  }
+  return m;
+}
 
 __global__ void __launch_bounds__(1024) plan_small_kernel(const uint8_t* __restrict__ mask, int64_t sb, int64_t sh,
                                                           int64_t srow, int mask_h, int nb, int rows_per_tile, int T,
                                                           int n, bool vec16, int32_t* __restrict__ tile_ptr,
                                                           int32_t* __restrict__ tile_col,
                                                           int32_t* __restrict__ tile_order) {
-  __shared__ int32_t cnt[kSmallPlanTiles];
-  __shared__ int32_t off[kSmallPlanTiles + 1];
+  // dynamic shared memory: [mask slices x nb x nb][cnt n][off n + 1][chunk bits n * cpr]
+  extern __shared__ __align__(16) uint8_t sm[];
   __shared__ int32_t warp_sums[32];
-  extern __shared__ uint8_t smask[];  // [slices][nb][nb]
   // the attention kernel that follows may start its set-up on the other SMs;
   // it waits for this kernel's completion before reading the plan
   allow_dependents();
   const int tid = threadIdx.x, lane = tid & 31, wid = tid >> 5;
-  const uint32_t lt_mask = (1u << lane) - 1u;
   const int slices = n / T;
   const int nn = nb * nb;  // <= kSmallPlanMaskBytes
   const int rows = slices * nb;
+  const int cpr = (nb + 15) / 16;
+  const int tasks = n * cpr;
+  uint8_t* smask = sm;
+  int32_t* cnt = reinterpret_cast<int32_t*>(sm + ((slices * nn + 15) & ~15));
+  int32_t* off = cnt + n;
+  uint32_t* kbits = reinterpret_cast<uint32_t*>(off + n + 1);
   if (vec16) {
     // 16-byte vectors: every load of the CTA is independent and coalesced
     const int vpr = nb / 16;
@@ -155,17 +179,20 @@ __global__ void __launch_bounds__(1024) plan_small_kernel(const uint8_t* __restr
       smask[i] = mask[static_cast<int64_t>(s / mask_h) * sb + static_cast<int64_t>(s % mask_h) * sh + r * srow + c];
     }
   }
+  for (int i = tid; i < n; i += 1024) cnt[i] = 0;
   __syncthreads();
-  // counts, one warp per tile
-  for (int w = wid; w < n; w += 32) {
-    const int s = w / T, t = w - (w / T) * T;
-    const uint8_t* base = smask + s * nn;
-    int count = 0;
-    for (int j0 = 0; j0 < nb; j0 += 32) {
-      const uint32_t f = tile_flags(base, nb, nb, rows_per_tile, t, j0 + lane);
-      count += __popc(__ballot_sync(0xffffffffu, f != 0));
-    }
-    if (lane == 0) cnt[w] = count;
+  // kept columns of each (tile, chunk): bits 0-15 first block row, 16-31 second
+  const bool aligned = nb % 16 == 0;
+  for (int task = tid; task < tasks; task += 1024) {
+    const int w = task / cpr, c = task - w * cpr;
+    const int s = w / T, t = w - s * T;
+    const int r0 = t * rows_per_tile;
+    const int jmax = nb - c * 16 < 16 ? nb - c * 16 : 16;
+    const uint8_t* base = smask + s * nn + c * 16;
+    const uint32_t m0 = nonzero_bits16(base + r0 * nb, jmax, aligned);
+    const uint32_t m1 = rows_per_tile == 2 && r0 + 1 < nb ? nonzero_bits16(base + (r0 + 1) * nb, jmax, aligned) : 0u;
+    kbits[task] = m0 | (m1 << 16);
+    atomicAdd(&cnt[w], __popc(m0 | m1));
   }
   __syncthreads();
   // exclusive scan: each thread a contiguous chunk, then warp and block totals
@@ -198,30 +225,44 @@ __global__ void __launch_bounds__(1024) plan_small_kernel(const uint8_t* __restr
   if (tid == 1023) off[n] = run;
   __syncthreads();
   for (int i = tid; i <= n; i += 1024) tile_ptr[i] = off[i];
-  // fill, one warp per tile
-  for (int w = wid; w < n; w += 32) {
-    const int s = w / T, t = w - (w / T) * T;
-    const uint8_t* base = smask + s * nn;
+  // fill: each chunk's entries in ascending column order
+  for (int task = tid; task < tasks; task += 1024) {
+    const int w = task / cpr, c = task - w * cpr;
+    const uint32_t kb = kbits[task];
     int pos = off[w];
-    for (int j0 = 0; j0 < nb; j0 += 32) {
-      const int j = j0 + lane;
-      const uint32_t f = tile_flags(base, nb, nb, rows_per_tile, t, j);
-      const uint32_t bal = __ballot_sync(0xffffffffu, f != 0);
-      if (f) tile_col[pos + __popc(bal & lt_mask)] = static_cast<int32_t>((f << 24) | static_cast<uint32_t>(j));
-      pos += __popc(bal);
+    for (int c2 = 0; c2 < c; ++c2) {
+      const uint32_t k2 = kbits[w * cpr + c2];
+      pos += __popc((k2 | (k2 >> 16)) & 0xFFFFu);
+    }
+    uint32_t kept = (kb | (kb >> 16)) & 0xFFFFu;
+    while (kept) {
+      const int k = __ffs(kept) - 1;
+      kept &= kept - 1;
+      const uint32_t f = rows_per_tile == 1 ? 3u : (((kb >> k) & 1u) | (((kb >> (16 + k)) & 1u) << 1));
+      tile_col[pos++] = static_cast<int32_t>((f << 24) | static_cast<uint32_t>(c * 16 + k));
     }
   }
-  // work order: rank by (decreasing count, increasing row) within the slice
+  // work order: rank by (decreasing count, increasing row) within the slice,
+  // g threads of one warp per tile
   if (tile_order) {
-    for (int w = tid; w < n; w += 1024) {
-      const int s0 = (w / T) * T, t = w - s0;
-      const int mine = cnt[w];
+    int g = 1;
+    while (g < 32 && 2 * g * n <= 1024) g *= 2;
+    const int gi = tid & (g - 1);
+    const int per_round = 1024 / g;
+    const int rounds = (n + per_round - 1) / per_round;
+    for (int rd = 0; rd < rounds; ++rd) {
+      const int w = rd * per_round + tid / g;
+      const bool valid = w < n;
+      const int s0 = valid ? (w / T) * T : 0, t = valid ? w - s0 : 0;
+      const int mine = valid ? cnt[w] : 0;
       int rank = 0;
-      for (int u = 0; u < T; ++u) {
-        const int c = cnt[s0 + u];
-        rank += (c > mine) || (c == mine && u < t);
-      }
-      tile_order[s0 + rank] = t;
+      if (valid)
+        for (int u = gi; u < T; u += g) {
+          const int c = cnt[s0 + u];
+          rank += (c > mine) || (c == mine && u < t);
+        }
+      for (int o = g / 2; o > 0; o >>= 1) rank += __shfl_xor_sync(0xffffffffu, rank, o);
+      if (valid && gi == 0) tile_order[s0 + rank] = t;
     }
   }
 }
@@ -450,18 +491,21 @@ extern "C" int bsa_build_plan(const uint8_t* mask, int64_t stride_b, int64_t str
   const int T = tiles_per_row(nb, block);
   const int64_t n = ptr_len - 1;
   const int64_t mask_bytes = static_cast<int64_t>(mask_b) * mask_h * nb * nb;
-  if (n <= kSmallPlanTiles && T <= kSmallPlanSliceTiles && mask_bytes <= kSmallPlanMaskBytes) {
+  const int64_t chunks = n * ((nb + 15) / 16);
+  if (n <= kSmallPlanTiles && T <= kSmallPlanSliceTiles && mask_bytes <= kSmallPlanMaskBytes &&
+      chunks <= kSmallPlanChunks) {
+    constexpr int kMaxDyn = kSmallPlanMaskBytes + 4 * (2 * kSmallPlanTiles + 1) + 4 * kSmallPlanChunks + 16;
     static bool attr_set[64];
     int dev = 0;
     if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return BSA_ERR_CUDA;
     if (!attr_set[dev]) {
-      BSA_CUDA_CHECK(
-          cudaFuncSetAttribute(plan_small_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmallPlanMaskBytes));
+      BSA_CUDA_CHECK(cudaFuncSetAttribute(plan_small_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kMaxDyn));
       attr_set[dev] = true;
     }
+    const size_t dyn = static_cast<size_t>((mask_bytes + 15) & ~int64_t(15)) + 4 * (2 * n + 1) + 4 * chunks;
     const bool vec16 = reinterpret_cast<uintptr_t>(mask) % 16 == 0 && nb % 16 == 0 && stride_row % 16 == 0 &&
                        (mask_b == 1 || stride_b % 16 == 0) && (mask_h == 1 || stride_h % 16 == 0);
-    plan_small_kernel<<<1, 1024, static_cast<size_t>(mask_bytes), st>>>(
+    plan_small_kernel<<<1, 1024, dyn, st>>>(
         mask, stride_b, stride_h, stride_row, mask_h, nb, 128 / block, T, static_cast<int>(n), vec16, tile_ptr,
         tile_col, tile_order);
     return cudaGetLastError() == cudaSuccess ? BSA_OK : BSA_ERR_CUDA;
