@@ -363,3 +363,30 @@ def test_reference_point_guard(dev, D, block):
     fin = np.isfinite(ref_lse)
     assert np.array_equal(np.isfinite(lv), fin)
     assert np.abs(lv[fin] - ref_lse[fin]).max() <= TOL_LSE * max(1.0, float(np.abs(ref_lse[fin]).max()) / 8)
+
+
+def test_concurrent_streams(dev):
+    """Forwards running at the same time on different streams: each launch
+    claims tiles from its own work-counter slot, so every result equals the
+    one computed alone (bitwise), also when the launches are repeated many
+    times (slots are reused after 64 launches)."""
+    B, H, N, D, block = 1, 4, 2048, 128, 128
+    nb = N // block
+    masks = [_rand_mask(nb, 0.2 + 0.1 * i, seed=60 + i, shape=(1, H)) for i in range(4)]
+    qkv = [_qkv(B, H, N, D, torch.bfloat16, seed=70 + i, dev=dev) for i in range(4)]
+    plans = [BlockSparsePlan(torch.from_numpy(m).to(dev), block) for m in masks]
+    alone = []
+    for (q, k, v), plan in zip(qkv, plans):
+        alone.append(block_sparse_attention(q, k, v, plan=plan, kernel="tcgen05"))
+    torch.cuda.synchronize()
+    streams = [torch.cuda.Stream(dev) for _ in range(4)]
+    outs = [torch.full_like(qkv[i][0], float("nan")) for i in range(4)]
+    for _ in range(40):
+        for i, st in enumerate(streams):
+            st.wait_stream(torch.cuda.current_stream(dev))
+            with torch.cuda.stream(st):
+                q, k, v = qkv[i]
+                block_sparse_attention(q, k, v, plan=plans[i], kernel="tcgen05", out=outs[i])
+        torch.cuda.synchronize()
+        for i in range(4):
+            assert torch.equal(outs[i], alone[i])
