@@ -390,3 +390,22 @@ def test_concurrent_streams(dev):
         torch.cuda.synchronize()
         for i in range(4):
             assert torch.equal(outs[i], alone[i])
+
+
+def test_long_context_sampled(dev):
+    """The long-context shape at full length (N = 65536, 512 block rows: the
+    mask is 256 KiB, so the plan takes the multi-kernel path, and each head has
+    512 tiles of ~72 kept blocks), two heads: sampled query blocks against the
+    oracle's block loop, lse included."""
+    wl = W.make("longctx")
+    q, k, v = (t[:, :2].contiguous() for t in wl.make_qkv(dev))
+    plan = BlockSparsePlan(wl.mask_tensor(dev), wl.block)
+    o, lse = block_sparse_attention(q, k, v, plan=plan, return_lse=True, check_errors=True)
+    qblocks = [0, 257, 511]
+    f = lambda t: t.float().cpu().numpy()  # noqa: E731
+    ref, ref_lse = OA.block_sparse_online(f(q), f(k), f(v), wl.mask[None, None], wl.block, query_blocks=qblocks)
+    got, gl = o.float().cpu().numpy(), lse.cpu().numpy()
+    for mb in qblocks:
+        r0, r1 = mb * wl.block, (mb + 1) * wl.block
+        assert np.abs(got[:, :, r0:r1] - ref[:, :, r0:r1]).max() <= TOL_16
+        assert np.abs(gl[:, :, r0:r1] - ref_lse[:, :, r0:r1]).max() <= TOL_LSE
