@@ -258,7 +258,8 @@ def run_ours(args):
     slices, nb = (ms[0] * ms[1], ms[-1]) if mask.dim() == 4 else (1, ms[-1])
     tiles_per_slice = (nb * wl.block + 127) // 128
     small = slices * tiles_per_slice <= 4096 and tiles_per_slice <= 1024 and slices * nb * nb <= 96 * 1024
-    launches_per_step = (1 if small else 4) + (2 if kp is not None else 0) + 1
+    # (BLOCK 64 launches two forms of the attention kernel; the plan's density picks the one that runs)
+    launches_per_step = (1 if small else 4) + (2 if kp is not None else 0) + (2 if wl.block == 64 else 1)
     k_events = []
 
     def step(record=False):

@@ -18,7 +18,7 @@
 //    kept block, V one block behind K because PV_g-1 is issued after S_g);
 //  * warp 1, one thread: tcgen05.mma issuer (S_g = Q K_g^T, then PV_g-1);
 //  * warpgroup 1: softmax, one query row per thread, P written back into
-//    the first BN/2 columns of S's TMEM;
+//    the first BS/2 columns of S's TMEM;
 //  * warpgroup 2: epilogue, one query row per thread: O / l from TMEM
 //    straight to global memory, lse, and the zero rows of empty tiles;
 //  * warps 2-3, with a query permutation only: gather the tile's Q rows
@@ -32,8 +32,9 @@
 // Buffers: S double-buffered in TMEM by global block counter g (S_g in
 // buffer g&1); O double-buffered by non-empty-tile counter e (O_e in buffer
 // e&1); Q double-buffered in shared memory by e; K and V in rings of KS and
-// VS stages.  TMEM columns: S0 [0,BN), S1 [BN,2BN), O0 [2BN,2BN+D),
-// O1 [2BN+D,2BN+2D).
+// VS stages; a step is 128 keys (one kept block at BLOCK 128, two at
+// BLOCK 64).  TMEM columns: S0 [0,BS), S1 [BS,2BS), O0 [2BS,2BS+D),
+// O1 [2BS+D,2BS+2D), BS = 128.
 // Ordering facts (one thread's tcgen05.mma operations execute in issue order
 // and tcgen05.commit tracks every earlier one):
 //  * S_g+2 reuses S_g's TMEM and is issued after PV_g, which reads P_g there;
@@ -60,6 +61,8 @@ namespace {
 constexpr int kWorkSlots = 64;
 __device__ uint32_t g_work_next[kWorkSlots];
 __device__ uint32_t g_work_done[kWorkSlots];
+// Launch counter shared by every instantiation of the kernel (they share the slots).
+std::atomic<unsigned> g_launches{0};
 
 constexpr int kTileRing = 8;   // tile numbers in flight between the producer and the other roles
 constexpr int kTileUsers = 11;  // MMA thread + 4 softmax + 4 epilogue + 2 Q-gather warps
@@ -79,7 +82,16 @@ struct TcpParams {
   int H, N, nb, T, mask_b, mask_h, total_tiles;
   int slot;  // work counter slot
   float scale_log2;
+  // 0: run.  1 / 2: run only if the plan averages at least / fewer than
+  // kPairMinEntries kept blocks per tile (the two forms launched for BLOCK 64).
+  int select;
 };
+
+// BLOCK 64: tiles averaging at least this many kept key blocks run the form
+// that takes them in pairs (128-key steps); sparser plans run one block per
+// step, where the shorter steps pipeline better (measured crossover between
+// 27 and 93 kept blocks per tile on causal masks).
+constexpr int kPairMinEntries = 32;
 
 constexpr int kSmemLimitP = 232448;
 constexpr int kThreadsP = 384;
@@ -96,14 +108,22 @@ __device__ __forceinline__ int64_t load_perm(const void* perm, int dtype, int64_
                                 : static_cast<int64_t>(__ldg(static_cast<const int32_t*>(perm) + i));
 }
 
-template <int D, int BN>
+// BN is the mask's block size (64 or 128).  A pipeline step covers BS keys:
+// one kept key block, or with PAIR (BN 64) two -- the tile's plan entries
+// taken in pairs, each 64-row box landing in one half of the stage -- so that
+// the S MMAs are 128 wide, the PV MMAs 128 deep, and the per-step hand-offs
+// between the roles are paid once per 128 keys.
+template <int D, int BN, bool PAIR>
 struct TcpCfg {
   static constexpr int BM = 128;
+  static constexpr int BS = PAIR ? 128 : BN;  // keys per step
+  static constexpr int SUB = BS / BN;   // plan entries per step
   static constexpr int NCHUNK = D / 64;
   static constexpr int Q_CHUNK = BM * 128;
-  static constexpr int KV_CHUNK = BN * 128;
+  static constexpr int KV_CHUNK = BS * 128;
+  static constexpr int BOX_BYTES = BN * 128;  // one entry's rows of one 64-column chunk
   static constexpr int Q_BYTES = BM * D * 2;
-  static constexpr int KV_BYTES = BN * D * 2;
+  static constexpr int KV_BYTES = BS * D * 2;
   static constexpr int BAR_BYTES = 512;
   static constexpr int STATS_BYTES = 2 * 2 * BM * 4;  // [buffer][m, l][row] fp32
   static constexpr bool fits(int ks, int vs) {
@@ -113,18 +133,19 @@ struct TcpCfg {
   static constexpr int KS = fits(4, 4) || fits(4, 3) ? 4 : 3;
   static constexpr int VS = fits(4, 4) ? 4 : fits(4, 3) ? 3 : 2;
   static constexpr int SMEM = 2 * Q_BYTES + (KS + VS) * KV_BYTES + BAR_BYTES + STATS_BYTES;
-  static constexpr int O_COL0 = 2 * BN;
-  static constexpr int TMEM_COLS = 2 * BN + 2 * D <= 256 ? 256 : 512;
+  static constexpr int O_COL0 = 2 * BS;
+  static constexpr int TMEM_COLS = 2 * BS + 2 * D <= 256 ? 256 : 512;
   static_assert(SMEM <= kSmemLimitP, "shared memory budget");
-  static_assert(2 * BN + 2 * D <= 512, "TMEM budget");
+  static_assert(2 * BS + 2 * D <= 512, "TMEM budget");
+  static_assert(SUB * BN == BS && (SUB == 1 || SUB == 2) && (!PAIR || BN == 64), "block size");
   static_assert((2 * KS + 2 * VS + 18 + 2 * kTileRing) * 8 + 8 + 4 * kTileRing <= BAR_BYTES, "barrier area");
 };
 
-template <int D, int BN, bool BF16>
+template <int D, int BN, bool BF16, bool PAIR>
 __global__ void __launch_bounds__(kThreadsP, 1)
     attn_tcp_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
                     const __grid_constant__ CUtensorMap tmV, const TcpParams p) {
-  using C = TcpCfg<D, BN>;
+  using C = TcpCfg<D, BN, PAIR>;
   constexpr int KS = C::KS, VS = C::VS;
   extern __shared__ __align__(1024) uint8_t smem[];
   if (smem_u32(smem) & 1023u) {
@@ -199,6 +220,17 @@ __global__ void __launch_bounds__(kThreadsP, 1)
   // before on the stream): everything above touched only this CTA's shared
   // memory and TMEM; from here on global memory is read and written.
   grid_dependency_wait();
+  if (p.select) {
+    // one of the two BLOCK 64 forms: every CTA reads the same plan total, so
+    // all take the same decision; the form not chosen frees TMEM and exits
+    // before it claims a tile
+    const int tiles = p.mask_b * p.mask_h * p.T;
+    const bool dense = __ldg(&p.tile_ptr[tiles]) >= kPairMinEntries * tiles;
+    if (dense != (p.select == 1)) {
+      if (warp == 1) tmem_dealloc(tmem, C::TMEM_COLS);
+      return;
+    }
+  }
 
   // tile w -> (entries e0 .. e0+n of the plan, b, h, tile row t)
   auto tile_info = [&](int w, int& e0, int& n, int& b, int& h, int& t) {
@@ -226,15 +258,19 @@ __global__ void __launch_bounds__(kThreadsP, 1)
       tma_prefetch_desc(&tmQ);
       tma_prefetch_desc(&tmK);
       tma_prefetch_desc(&tmV);
-      int e = 0, g = 0, gv = 0;           // non-empty tiles, K loads, V loads so far
-      int pv_b = 0, pv_h = 0, pv_kb = 0;  // the block whose V is still to load (gv < g)
+      int e = 0, g = 0, gv = 0;  // non-empty tiles, K steps, V steps loaded so far
+      int pv_b = 0, pv_h = 0;    // the step whose V is still to load (gv < g)
+      int pv_kb[C::SUB] = {};
       bool ok = true;
       auto load_v = [&]() -> bool {
         const int st = gv % VS;
         if (gv >= VS && !mbar_wait(&v_empty[st], ((gv / VS) - 1) & 1, abort_flag, p.err)) return false;
         mbar_arrive_expect_tx(&v_full[st], C::KV_BYTES);
-        for (int c = 0; c < C::NCHUNK; ++c)
-          tma_load_4d(sV + st * C::KV_BYTES + c * C::KV_CHUNK, &tmV, &v_full[st], c * 64, pv_kb * BN, pv_h, pv_b);
+#pragma unroll
+        for (int u = 0; u < C::SUB; ++u)
+          for (int c = 0; c < C::NCHUNK; ++c)
+            tma_load_4d(sV + st * C::KV_BYTES + c * C::KV_CHUNK + u * C::BOX_BYTES, &tmV, &v_full[st], c * 64,
+                        pv_kb[u] * BN, pv_h, pv_b);
         ++gv;
         return true;
       };
@@ -258,21 +294,32 @@ __global__ void __launch_bounds__(kThreadsP, 1)
             tma_load_4d(sQ + qb * C::Q_BYTES + c * C::Q_CHUNK, &tmQ, &q_full[qb], c * 64, t * 128, h, b);
         }
         ++e;
-        for (int j = 0; j < n; ++j, ++g) {
+        const int nsteps = (n + C::SUB - 1) / C::SUB;
+        for (int j = 0; j < nsteps; ++j, ++g) {
           const int st = g % KS;
           if (g >= KS && !(ok = mbar_wait(&k_empty[st], ((g / KS) - 1) & 1, abort_flag, p.err))) break;
-          int kb = static_cast<int>(static_cast<uint32_t>(p.tile_col[e0 + j]) & 0xFFFFFFu);
-          if (kb >= p.nb) {
-            set_err(p.err, BSA_DEVERR_PLAN);
-            kb = 0;
+          int kb[C::SUB];
+#pragma unroll
+          for (int u = 0; u < C::SUB; ++u) {
+            // a missing second entry (odd count) repeats the first: the softmax masks it out
+            const int ei = j * C::SUB + u < n ? j * C::SUB + u : j * C::SUB;
+            kb[u] = static_cast<int>(static_cast<uint32_t>(p.tile_col[e0 + ei]) & 0xFFFFFFu);
+            if (kb[u] >= p.nb) {
+              set_err(p.err, BSA_DEVERR_PLAN);
+              kb[u] = 0;
+            }
           }
           mbar_arrive_expect_tx(&k_full[st], C::KV_BYTES);
-          for (int c = 0; c < C::NCHUNK; ++c)
-            tma_load_4d(sK + st * C::KV_BYTES + c * C::KV_CHUNK, &tmK, &k_full[st], c * 64, kb * BN, h, b);
+#pragma unroll
+          for (int u = 0; u < C::SUB; ++u)
+            for (int c = 0; c < C::NCHUNK; ++c)
+              tma_load_4d(sK + st * C::KV_BYTES + c * C::KV_CHUNK + u * C::BOX_BYTES, &tmK, &k_full[st], c * 64,
+                          kb[u] * BN, h, b);
           if (gv < g && !(ok = load_v())) break;
           pv_b = b;
           pv_h = h;
-          pv_kb = kb;
+#pragma unroll
+          for (int u = 0; u < C::SUB; ++u) pv_kb[u] = kb[u];
         }
       }
       if (ok && gv < g) ok = load_v();
@@ -282,7 +329,7 @@ __global__ void __launch_bounds__(kThreadsP, 1)
       }
     } else if (warp == 1 && lane == 0) {
       // ------------------------------------------------------------ MMA issuer
-      constexpr uint32_t idesc_qk = make_idesc_f16(BF16, 128, BN, false, false);
+      constexpr uint32_t idesc_qk = make_idesc_f16(BF16, 128, C::BS, false, false);
       constexpr uint32_t idesc_pv = make_idesc_f16(BF16, 128, D, false, true);
       const uint32_t q_addr = smem_u32(sQ);
       const uint32_t k_addr = smem_u32(sK);
@@ -302,10 +349,10 @@ __global__ void __launch_bounds__(kThreadsP, 1)
         if (!mbar_wait(&p_ready[i & 1], (i >> 1) & 1, abort_flag, p.err)) return false;
         if (!mbar_wait(&v_full[st], (i / VS) & 1, abort_flag, p.err)) return false;
         tc_fence_after();
-        const uint32_t p_tmem = tmem + (i & 1) * BN;  // P_i lives in the first columns of S buffer i&1
+        const uint32_t p_tmem = tmem + (i & 1) * C::BS;  // P_i lives in the first columns of S buffer i&1
         const uint32_t o_tmem = tmem + C::O_COL0 + pend_ob * D;
 #pragma unroll
-        for (int kk = 0; kk < BN / 16; ++kk) {
+        for (int kk = 0; kk < C::BS / 16; ++kk) {
           const uint64_t bd = make_sw128_desc(v_addr + st * C::KV_BYTES + kk * 16 * 128, C::KV_CHUNK, 1024);
           tc_mma_ts(o_tmem, p_tmem + kk * 8, bd, idesc_pv, (!pend_first || kk > 0) ? 1u : 0u);
         }
@@ -326,11 +373,12 @@ __global__ void __launch_bounds__(kThreadsP, 1)
         const int qb = e & 1;
         if (!(ok = mbar_wait(&q_full[qb], (e >> 1) & 1, abort_flag, p.err))) break;
         tc_fence_after();
-        for (int j = 0; j < n; ++j, ++jg) {
+        const int nsteps = (n + C::SUB - 1) / C::SUB;
+        for (int j = 0; j < nsteps; ++j, ++jg) {
           const int st = jg % KS;
           if (!(ok = mbar_wait(&k_full[st], (jg / KS) & 1, abort_flag, p.err))) break;
           tc_fence_after();
-          const uint32_t d_tmem = tmem + (jg & 1) * BN;
+          const uint32_t d_tmem = tmem + (jg & 1) * C::BS;
 #pragma unroll
           for (int kk = 0; kk < D / 16; ++kk) {
             const uint32_t off = (kk & 3) * 32;  // 16 elements = 32 bytes inside the 128-byte swizzle row
@@ -340,12 +388,12 @@ __global__ void __launch_bounds__(kThreadsP, 1)
           }
           tc_commit(&s_full[jg & 1]);
           tc_commit(&k_empty[st]);
-          if (j == n - 1) tc_commit(&q_empty[qb]);
+          if (j == nsteps - 1) tc_commit(&q_empty[qb]);
           if (pend_j >= 0 && !(ok = do_pv())) break;
           pend_j = jg;
           pend_ob = e & 1;
           pend_first = j == 0;
-          pend_last = j == n - 1;
+          pend_last = j == nsteps - 1;
         }
         ++e;
       }
@@ -417,31 +465,42 @@ __global__ void __launch_bounds__(kThreadsP, 1)
       if (n == 0) continue;  // the epilogue writes its zero rows
       const int ob = e & 1;
       float m_run = -INFINITY, l_run = 0.f;
-      for (int j = 0; j < n; ++j, ++jg) {
+      const int nsteps = (n + C::SUB - 1) / C::SUB;
+      for (int j = 0; j < nsteps; ++j, ++jg) {
         const int sb = jg & 1;
         // after a failed wait every later wait returns at once (abort flag)
         if (!(ok = ok && __all_sync(0xffffffffu, mbar_wait(&s_full[sb], (jg >> 1) & 1, abort_flag, p.err))))
           continue;
         tc_fence_after();
-        uint32_t sr[BN];
+        uint32_t sr[C::BS];
 #pragma unroll
-        for (int c = 0; c < BN / 32; ++c) tmem_ld32(lane_base + sb * BN + c * 32, &sr[c * 32]);
+        for (int c = 0; c < C::BS / 32; ++c) tmem_ld32(lane_base + sb * C::BS + c * 32, &sr[c * 32]);
         tmem_wait_ld();
-        const uint32_t entry = static_cast<uint32_t>(__ldg(&p.tile_col[e0 + j]));
-        const bool active = BN == 128 ? true : (((entry >> 24 >> half) & 1u) != 0);
-        {
-          // keys at or past N (a partial last key block; TMA zero-filled them) are
-          // masked out: only the one block that crosses N takes this branch
-          const int kvalid = p.N - static_cast<int>(entry & 0xFFFFFFu) * BN;
-          if (kvalid < BN) {
+        // Per plan entry of the step: whether this row's query block keeps it
+        // (per-half flags at BN 64; a missing second entry is never kept) and
+        // how many of its keys lie before N (TMA zero-filled the rest).
+        bool act[C::SUB];
+        int kvalid[C::SUB];
+        bool any = false, need_mask = false;
 #pragma unroll
-            for (int i = 0; i < BN; ++i)
-              if (i >= kvalid) sr[i] = __float_as_uint(-INFINITY);
-          }
+        for (int u = 0; u < C::SUB; ++u) {
+          const int ei = j * C::SUB + u;
+          const uint32_t entry = ei < n ? static_cast<uint32_t>(__ldg(&p.tile_col[e0 + ei])) : 0u;
+          act[u] = ei < n && (BN == 128 || ((entry >> 24 >> half) & 1u) != 0);
+          kvalid[u] = p.N - static_cast<int>(entry & 0xFFFFFFu) * BN;
+          any = any || act[u];
+          need_mask = need_mask || !act[u] || kvalid[u] < BN;
         }
-        uint32_t pr[BN / 2];
-        if (active) {
-          const float alpha = softmax_block<BN, BF16>(sr, pr, p.scale_log2, m_run, l_run);
+        uint32_t pr[C::BS / 2];
+        if (any) {
+          if (need_mask) {  // (uniform per warp: a warp's 32 rows share a query block)
+#pragma unroll
+            for (int i = 0; i < C::BS; ++i) {
+              const int u = i / BN;
+              if (!act[u] || i - u * BN >= kvalid[u]) sr[i] = __float_as_uint(-INFINITY);
+            }
+          }
+          const float alpha = softmax_block<C::BS, BF16>(sr, pr, p.scale_log2, m_run, l_run);
           if (__any_sync(0xffffffffu, alpha != 1.f)) {
             // O holds the sum up to block j-1 of this tile: wait for that PV, rescale in TMEM.
             if (!(ok = __all_sync(0xffffffffu, mbar_wait(pv_done, (jg - 1) & 1, abort_flag, p.err)))) continue;
@@ -458,11 +517,11 @@ __global__ void __launch_bounds__(kThreadsP, 1)
           }
         } else {
 #pragma unroll
-          for (int i = 0; i < BN / 2; ++i) pr[i] = 0u;
+          for (int i = 0; i < C::BS / 2; ++i) pr[i] = 0u;
         }
-        // P_j into the first BN/2 columns of its S buffer (all of S is in registers)
+        // P_j into the first BS/2 columns of its S buffer (all of S is in registers)
 #pragma unroll
-        for (int c = 0; c < BN / 64; ++c) tmem_st32(lane_base + sb * BN + c * 32, &pr[c * 32]);
+        for (int c = 0; c < C::BS / 64; ++c) tmem_st32(lane_base + sb * C::BS + c * 32, &pr[c * 32]);
         tmem_wait_st();
         tc_fence_before();
         __syncwarp();
@@ -584,10 +643,10 @@ int sm_count() {
   return count[dev];
 }
 
-template <int D, int BN, bool BF16>
-int launch_p(const bsa_fwd_args* a, cudaStream_t st, const void* q_perm, int perm_dtype) {
-  using C = TcpCfg<D, BN>;
-  auto kern = attn_tcp_kernel<D, BN, BF16>;
+template <int D, int BN, bool BF16, bool PAIR>
+int launch_p(const bsa_fwd_args* a, cudaStream_t st, const void* q_perm, int perm_dtype, int select) {
+  using C = TcpCfg<D, BN, PAIR>;
+  auto kern = attn_tcp_kernel<D, BN, BF16, PAIR>;
   // The setmaxnreg split needs the launch to hold at least the sum of the
   // three warpgroups' shares; with fewer the increase would never be granted.
   static int checked = 0;  // 1 ok, 2 too few registers
@@ -626,8 +685,8 @@ int launch_p(const bsa_fwd_args* a, cudaStream_t st, const void* q_perm, int per
   p.mask_h = a->plan.mask_h;
   p.total_tiles = a->B * a->H * p.T;
   p.scale_log2 = a->sm_scale * 1.4426950408889634f;
-  static std::atomic<unsigned> launches{0};
-  p.slot = static_cast<int>(launches.fetch_add(1, std::memory_order_relaxed) % kWorkSlots);
+  p.select = select;
+  p.slot = static_cast<int>(g_launches.fetch_add(1, std::memory_order_relaxed) % kWorkSlots);
   BSA_CUDA_CHECK(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM));
   int grid = sm_count();
   if (grid > p.total_tiles) grid = p.total_tiles;
@@ -653,10 +712,21 @@ int launch_p(const bsa_fwd_args* a, cudaStream_t st, const void* q_perm, int per
 int launch_attn_tcp(const bsa_fwd_args* a, cudaStream_t st, const void* q_perm, int perm_dtype) {
   const bool bf16 = a->dtype == BSA_DTYPE_BF16;
   const int bn = a->plan.block;
-#define BSA_TCP_CASE(D_, BN_)                                                          \
-  if (a->D == D_ && bn == BN_)                                                         \
-    return bf16 ? launch_p<D_, BN_, true>(a, st, q_perm, perm_dtype) \
-                : launch_p<D_, BN_, false>(a, st, q_perm, perm_dtype);
+  // BLOCK 64: both forms are launched back to back and the plan's density
+  // (read on the device, no host synchronisation) picks the one that runs.
+#define BSA_TCP_CASE(D_, BN_)                                                                     \
+  if (a->D == D_ && bn == BN_) {                                                                  \
+    if constexpr (BN_ == 128)                                                                     \
+      return bf16 ? launch_p<D_, BN_, true, false>(a, st, q_perm, perm_dtype, 0)                  \
+                  : launch_p<D_, BN_, false, false>(a, st, q_perm, perm_dtype, 0);                \
+    else {                                                                                        \
+      int r_ = bf16 ? launch_p<D_, BN_, true, true>(a, st, q_perm, perm_dtype, 1)                 \
+                    : launch_p<D_, BN_, false, true>(a, st, q_perm, perm_dtype, 1);               \
+      if (r_) return r_;                                                                          \
+      return bf16 ? launch_p<D_, BN_, true, false>(a, st, q_perm, perm_dtype, 2)                  \
+                  : launch_p<D_, BN_, false, false>(a, st, q_perm, perm_dtype, 2);                \
+    }                                                                                             \
+  }
   BSA_TCP_CASE(64, 64)
   BSA_TCP_CASE(64, 128)
   BSA_TCP_CASE(128, 64)

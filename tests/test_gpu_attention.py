@@ -409,3 +409,42 @@ def test_long_context_sampled(dev):
         r0, r1 = mb * wl.block, (mb + 1) * wl.block
         assert np.abs(got[:, :, r0:r1] - ref[:, :, r0:r1]).max() <= TOL_16
         assert np.abs(gl[:, :, r0:r1] - ref_lse[:, :, r0:r1]).max() <= TOL_LSE
+
+
+@pytest.mark.parametrize("D", [64, 128])
+def test_block64_steps_pair_entries(dev, D):
+    """At BLOCK 64 the kernel takes a tile's kept key blocks two at a time
+    (one 128-key step).  Covered here: tiles with an odd number of kept
+    blocks (the last step has one), blocks kept by only one of the tile's two
+    query block rows, a tile whose rows keep disjoint blocks, a partial last
+    key block (N % 64 != 0) in either half of a step, and key blocks no query
+    keeps filled with NaN."""
+    B, H, block = 1, 3, 64
+    N = 64 * 13 + 23
+    nb = (N + block - 1) // block
+    rng = np.random.default_rng(D)
+    mask = rng.random((1, H, nb, nb)) < 0.3
+    mask[..., np.arange(nb), np.arange(nb)] = True
+    mask[:, 0, 2, :] = False                       # rows 2 and 3 (one tile) keep disjoint blocks
+    mask[:, 0, 3, :] = False
+    mask[:, 0, 2, [0, 5, 9]] = True
+    mask[:, 0, 3, [1, 4, 13]] = True
+    mask[:, 1, 4, :] = False                       # row 4 keeps only the partial last block,
+    mask[:, 1, 4, nb - 1] = True                   # row 5 keeps three blocks: odd count in the tile
+    mask[:, 1, 5, :] = False
+    mask[:, 1, 5, [0, 7, nb - 1]] = True
+    mask[:, 2, :, 11] = False                      # head 2: block 11 kept by nobody -> NaN keys and values
+    q, k, v = _qkv(B, H, N, D, torch.bfloat16, seed=D + 5, dev=dev)
+    k[:, 2, 11 * block:12 * block] = float("nan")
+    v[:, 2, 11 * block:12 * block] = float("nan")
+    plan = BlockSparsePlan(torch.from_numpy(mask).to(dev), block)
+    o, lse = block_sparse_attention(q, k, v, plan=plan, kernel="tcgen05", return_lse=True, check_errors=True)
+    kc, vc = k.clone(), v.clone()
+    kc[:, 2, 11 * block:12 * block] = 0
+    vc[:, 2, 11 * block:12 * block] = 0
+    ref_o, ref_lse = _torch_masked_reference(q, kc, vc, mask, block, 1.0 / math.sqrt(D))
+    assert torch.isfinite(o).all()
+    assert (o.float() - ref_o).abs().max().item() <= TOL_16
+    fin = torch.isfinite(ref_lse)
+    assert torch.equal(torch.isfinite(lse), fin)
+    assert (lse[fin] - ref_lse[fin]).abs().max().item() <= TOL_LSE
