@@ -220,15 +220,17 @@ __global__ void __launch_bounds__(kThreadsP, 1)
   // before on the stream): everything above touched only this CTA's shared
   // memory and TMEM; from here on global memory is read and written.
   grid_dependency_wait();
-  if (p.select) {
-    // one of the two BLOCK 64 forms: every CTA reads the same plan total, so
-    // all take the same decision; the form not chosen frees TMEM and exits
-    // before it claims a tile
-    const int tiles = p.mask_b * p.mask_h * p.T;
-    const bool dense = __ldg(&p.tile_ptr[tiles]) >= kPairMinEntries * tiles;
-    if (dense != (p.select == 1)) {
-      if (warp == 1) tmem_dealloc(tmem, C::TMEM_COLS);
-      return;
+  if constexpr (BN == 64) {
+    if (p.select) {
+      // one of the two BLOCK 64 forms: every CTA reads the same plan total, so
+      // all take the same decision; the form not chosen frees TMEM and exits
+      // before it claims a tile
+      const int tiles = p.mask_b * p.mask_h * p.T;
+      const bool dense = __ldg(&p.tile_ptr[tiles]) >= kPairMinEntries * tiles;
+      if (dense != (p.select == 1)) {
+        if (warp == 1) tmem_dealloc(tmem, C::TMEM_COLS);
+        return;
+      }
     }
   }
 
