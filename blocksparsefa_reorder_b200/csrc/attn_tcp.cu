@@ -39,7 +39,9 @@
 // and tcgen05.commit tracks every earlier one):
 //  * S_g+2 reuses S_g's TMEM and is issued after PV_g, which reads P_g there;
 //  * S_g complete implies PV_g-2 complete, and PV_g-1 completes before any
-//    later MMA: the softmax's rescale of O waits pv_done for PV_g-1;
+//    later MMA: the softmax's rescale of O waits step_done of PV_g-1;
+//  * one commit per step (step_done[g % 4], after PV_g) frees K and V
+//    stages: it tracks S_g+1 (issued before PV_g) and PV_g;
 //  * Q_e's buffer is released (q_empty) by a commit after the tile's last S;
 //  * the first PV of tile e+2 waits o_empty[e&1]: the epilogue has read O_e.
 // Every wait is bounded by %globaltimer; a timeout sets BSA_DEVERR_TIMEOUT
@@ -138,7 +140,7 @@ struct TcpCfg {
   static_assert(SMEM <= kSmemLimitP, "shared memory budget");
   static_assert(2 * BS + 2 * D <= 512, "TMEM budget");
   static_assert(SUB * BN == BS && (SUB == 1 || SUB == 2) && (!PAIR || BN == 64), "block size");
-  static_assert((2 * KS + 2 * VS + 18 + 2 * kTileRing) * 8 + 8 + 4 * kTileRing <= BAR_BYTES, "barrier area");
+  static_assert((KS + VS + 21 + 2 * kTileRing) * 8 + 8 + 4 * kTileRing <= BAR_BYTES, "barrier area");
 };
 
 template <int D, int BN, bool BF16, bool PAIR>
@@ -160,17 +162,17 @@ __global__ void __launch_bounds__(kThreadsP, 1)
   uint64_t* q_full = bars;               // [2]
   uint64_t* q_empty = q_full + 2;        // [2] the tile's last S has read Q
   uint64_t* k_full = q_empty + 2;        // [KS]
-  uint64_t* k_empty = k_full + KS;       // [KS] S MMA has read K
-  uint64_t* v_full = k_empty + KS;       // [VS]
-  uint64_t* v_empty = v_full + VS;       // [VS] PV MMA has read V
-  uint64_t* s_full = v_empty + VS;       // [2] by S buffer
+  uint64_t* v_full = k_full + KS;        // [VS]
+  uint64_t* s_full = v_full + VS;        // [2] by S buffer
   uint64_t* p_ready = s_full + 2;        // [2] by S buffer, 4 softmax warps
   uint64_t* o_final = p_ready + 2;       // [2] by O buffer: the tile's last PV completed
   uint64_t* o_empty = o_final + 2;       // [2] by O buffer: 4 epilogue warps read O
   uint64_t* stats_ready = o_empty + 2;   // [2] 4 softmax warps wrote (m, l)
   uint64_t* stats_empty = stats_ready + 2;  // [2] 4 epilogue warps read (m, l)
-  uint64_t* pv_done = stats_empty + 2;   // one phase per PV
-  uint64_t* drain = pv_done + 1;
+  // [4] by step g % 4: one commit after PV_g tracks PV_g and every earlier MMA
+  // (S_g+1 among them): it frees K and V stages and lets a rescale of O go ahead
+  uint64_t* step_done = stats_empty + 2;
+  uint64_t* drain = step_done + 4;
   uint64_t* tile_ready = drain + 1;              // [kTileRing] producer wrote the entry
   uint64_t* tile_free = tile_ready + kTileRing;  // [kTileRing] all kTileUsers read it
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(tile_free + kTileRing);
@@ -191,15 +193,9 @@ __global__ void __launch_bounds__(kThreadsP, 1)
       mbar_init(&stats_ready[i], 4);
       mbar_init(&stats_empty[i], 4);
     }
-    for (int i = 0; i < KS; ++i) {
-      mbar_init(&k_full[i], 1);
-      mbar_init(&k_empty[i], 1);
-    }
-    for (int i = 0; i < VS; ++i) {
-      mbar_init(&v_full[i], 1);
-      mbar_init(&v_empty[i], 1);
-    }
-    mbar_init(pv_done, 1);
+    for (int i = 0; i < KS; ++i) mbar_init(&k_full[i], 1);
+    for (int i = 0; i < VS; ++i) mbar_init(&v_full[i], 1);
+    for (int i = 0; i < 4; ++i) mbar_init(&step_done[i], 1);
     mbar_init(drain, 1);
     for (int i = 0; i < kTileRing; ++i) {
       mbar_init(&tile_ready[i], 1);
@@ -266,7 +262,8 @@ __global__ void __launch_bounds__(kThreadsP, 1)
       bool ok = true;
       auto load_v = [&]() -> bool {
         const int st = gv % VS;
-        if (gv >= VS && !mbar_wait(&v_empty[st], ((gv / VS) - 1) & 1, abort_flag, p.err)) return false;
+        // V_gv-VS's stage is free once PV_gv-VS completed
+        if (gv >= VS && !mbar_wait(&step_done[(gv - VS) & 3], ((gv - VS) >> 2) & 1, abort_flag, p.err)) return false;
         mbar_arrive_expect_tx(&v_full[st], C::KV_BYTES);
 #pragma unroll
         for (int u = 0; u < C::SUB; ++u)
@@ -299,7 +296,10 @@ __global__ void __launch_bounds__(kThreadsP, 1)
         const int nsteps = (n + C::SUB - 1) / C::SUB;
         for (int j = 0; j < nsteps; ++j, ++g) {
           const int st = g % KS;
-          if (g >= KS && !(ok = mbar_wait(&k_empty[st], ((g / KS) - 1) & 1, abort_flag, p.err))) break;
+          // K_g-KS's stage is free once S_g-KS completed: the commit after PV_g-KS-1
+          // (S_0 and S_1 both under the one after PV_0)
+          const int sd = g - KS - 1 > 0 ? g - KS - 1 : 0;
+          if (g >= KS && !(ok = mbar_wait(&step_done[sd & 3], (sd >> 2) & 1, abort_flag, p.err))) break;
           int kb[C::SUB];
 #pragma unroll
           for (int u = 0; u < C::SUB; ++u) {
@@ -358,8 +358,7 @@ __global__ void __launch_bounds__(kThreadsP, 1)
           const uint64_t bd = make_sw128_desc(v_addr + st * C::KV_BYTES + kk * 16 * 128, C::KV_CHUNK, 1024);
           tc_mma_ts(o_tmem, p_tmem + kk * 8, bd, idesc_pv, (!pend_first || kk > 0) ? 1u : 0u);
         }
-        tc_commit(&v_empty[st]);
-        tc_commit(pv_done);
+        tc_commit(&step_done[i & 3]);
         if (pend_last) tc_commit(&o_final[pend_ob]);
         if (pend_first) ++pv_issued_tiles;
         pend_j = -1;
@@ -389,7 +388,6 @@ __global__ void __launch_bounds__(kThreadsP, 1)
             tc_mma_ss(d_tmem, a, bd, idesc_qk, kk > 0 ? 1u : 0u);
           }
           tc_commit(&s_full[jg & 1]);
-          tc_commit(&k_empty[st]);
           if (j == nsteps - 1) tc_commit(&q_empty[qb]);
           if (pend_j >= 0 && !(ok = do_pv())) break;
           pend_j = jg;
@@ -505,7 +503,9 @@ __global__ void __launch_bounds__(kThreadsP, 1)
           const float alpha = softmax_block<C::BS, BF16>(sr, pr, p.scale_log2, m_run, l_run);
           if (__any_sync(0xffffffffu, alpha != 1.f)) {
             // O holds the sum up to block j-1 of this tile: wait for that PV, rescale in TMEM.
-            if (!(ok = __all_sync(0xffffffffu, mbar_wait(pv_done, (jg - 1) & 1, abort_flag, p.err)))) continue;
+            if (!(ok = __all_sync(0xffffffffu,
+                                  mbar_wait(&step_done[(jg - 1) & 3], ((jg - 1) >> 2) & 1, abort_flag, p.err))))
+              continue;
             tc_fence_after();
 #pragma unroll
             for (int c = 0; c < D / 32; ++c) {
