@@ -15,7 +15,8 @@
 // shared memory.  The counter is one of kWorkSlots per device, taken in turn
 // by successive launches; the last CTA to finish resets it.  Roles:
 //  * warp 0, one thread: TMA producer (Q per tile, then K_g and V_g-1 per
-//    kept block, V one block behind K because PV_g-1 is issued after S_g);
+//    step, V one step behind K because PV_g-1 is issued after S_g; both land
+//    on one barrier, so the MMA issuer waits once per step for its data);
 //  * warp 1, one thread: tcgen05.mma issuer (S_g = Q K_g^T, then PV_g-1);
 //  * warpgroup 1: softmax, one query row per thread, P written back into
 //    the first BS/2 columns of S's TMEM;
@@ -140,7 +141,7 @@ struct TcpCfg {
   static_assert(SMEM <= kSmemLimitP, "shared memory budget");
   static_assert(2 * BS + 2 * D <= 512, "TMEM budget");
   static_assert(SUB * BN == BS && (SUB == 1 || SUB == 2) && (!PAIR || BN == 64), "block size");
-  static_assert((KS + VS + 21 + 2 * kTileRing) * 8 + 8 + 4 * kTileRing <= BAR_BYTES, "barrier area");
+  static_assert((KS + 21 + 2 * kTileRing) * 8 + 8 + 4 * kTileRing <= BAR_BYTES, "barrier area");
 };
 
 template <int D, int BN, bool BF16, bool PAIR>
@@ -161,9 +162,9 @@ __global__ void __launch_bounds__(kThreadsP, 1)
   float* stats = reinterpret_cast<float*>(reinterpret_cast<uint8_t*>(bars) + C::BAR_BYTES);
   uint64_t* q_full = bars;               // [2]
   uint64_t* q_empty = q_full + 2;        // [2] the tile's last S has read Q
-  uint64_t* k_full = q_empty + 2;        // [KS]
-  uint64_t* v_full = k_full + KS;        // [VS]
-  uint64_t* s_full = v_full + VS;        // [2] by S buffer
+  // [KS] by step g % KS: K_g and V_g-1 (issued together) have landed
+  uint64_t* kv_full = q_empty + 2;
+  uint64_t* s_full = kv_full + KS;       // [2] by S buffer
   uint64_t* p_ready = s_full + 2;        // [2] by S buffer, 4 softmax warps
   uint64_t* o_final = p_ready + 2;       // [2] by O buffer: the tile's last PV completed
   uint64_t* o_empty = o_final + 2;       // [2] by O buffer: 4 epilogue warps read O
@@ -193,8 +194,7 @@ __global__ void __launch_bounds__(kThreadsP, 1)
       mbar_init(&stats_ready[i], 4);
       mbar_init(&stats_empty[i], 4);
     }
-    for (int i = 0; i < KS; ++i) mbar_init(&k_full[i], 1);
-    for (int i = 0; i < VS; ++i) mbar_init(&v_full[i], 1);
+    for (int i = 0; i < KS; ++i) mbar_init(&kv_full[i], 1);
     for (int i = 0; i < 4; ++i) mbar_init(&step_done[i], 1);
     mbar_init(drain, 1);
     for (int i = 0; i < kTileRing; ++i) {
@@ -260,15 +260,22 @@ __global__ void __launch_bounds__(kThreadsP, 1)
       int pv_b = 0, pv_h = 0;    // the step whose V is still to load (gv < g)
       int pv_kb[C::SUB] = {};
       bool ok = true;
-      auto load_v = [&]() -> bool {
+      int armed = 0;  // kv_full phases armed so far (one per step, one more for the last V)
+      // the barrier of step gs's K may be re-armed once S_gs-KS completed: the commit
+      // after PV_gs-KS-1 (S_0 and S_1 both under the one after PV_0)
+      auto wait_k_stage = [&](int gs) -> bool {
+        const int sd = gs - KS - 1 > 0 ? gs - KS - 1 : 0;
+        return gs < KS || mbar_wait(&step_done[sd & 3], (sd >> 2) & 1, abort_flag, p.err);
+      };
+      // V_gv into its stage, counted on the barrier of the step it travels with (bar)
+      auto load_v = [&](uint64_t* bar) -> bool {
         const int st = gv % VS;
         // V_gv-VS's stage is free once PV_gv-VS completed
         if (gv >= VS && !mbar_wait(&step_done[(gv - VS) & 3], ((gv - VS) >> 2) & 1, abort_flag, p.err)) return false;
-        mbar_arrive_expect_tx(&v_full[st], C::KV_BYTES);
 #pragma unroll
         for (int u = 0; u < C::SUB; ++u)
           for (int c = 0; c < C::NCHUNK; ++c)
-            tma_load_4d(sV + st * C::KV_BYTES + c * C::KV_CHUNK + u * C::BOX_BYTES, &tmV, &v_full[st], c * 64,
+            tma_load_4d(sV + st * C::KV_BYTES + c * C::KV_CHUNK + u * C::BOX_BYTES, &tmV, bar, c * 64,
                         pv_kb[u] * BN, pv_h, pv_b);
         ++gv;
         return true;
@@ -296,10 +303,7 @@ __global__ void __launch_bounds__(kThreadsP, 1)
         const int nsteps = (n + C::SUB - 1) / C::SUB;
         for (int j = 0; j < nsteps; ++j, ++g) {
           const int st = g % KS;
-          // K_g-KS's stage is free once S_g-KS completed: the commit after PV_g-KS-1
-          // (S_0 and S_1 both under the one after PV_0)
-          const int sd = g - KS - 1 > 0 ? g - KS - 1 : 0;
-          if (g >= KS && !(ok = mbar_wait(&step_done[sd & 3], (sd >> 2) & 1, abort_flag, p.err))) break;
+          if (!(ok = wait_k_stage(g))) break;
           int kb[C::SUB];
 #pragma unroll
           for (int u = 0; u < C::SUB; ++u) {
@@ -311,23 +315,32 @@ __global__ void __launch_bounds__(kThreadsP, 1)
               kb[u] = 0;
             }
           }
-          mbar_arrive_expect_tx(&k_full[st], C::KV_BYTES);
+          // K_g and (from the second step on) V_g-1 complete one phase of kv_full[st]
+          mbar_arrive_expect_tx(&kv_full[st], gv < g ? 2 * C::KV_BYTES : C::KV_BYTES);
+          ++armed;
 #pragma unroll
           for (int u = 0; u < C::SUB; ++u)
             for (int c = 0; c < C::NCHUNK; ++c)
-              tma_load_4d(sK + st * C::KV_BYTES + c * C::KV_CHUNK + u * C::BOX_BYTES, &tmK, &k_full[st], c * 64,
+              tma_load_4d(sK + st * C::KV_BYTES + c * C::KV_CHUNK + u * C::BOX_BYTES, &tmK, &kv_full[st], c * 64,
                           kb[u] * BN, h, b);
-          if (gv < g && !(ok = load_v())) break;
+          if (gv < g && !(ok = load_v(&kv_full[st]))) break;
           pv_b = b;
           pv_h = h;
 #pragma unroll
           for (int u = 0; u < C::SUB; ++u) pv_kb[u] = kb[u];
         }
       }
-      if (ok && gv < g) ok = load_v();
+      if (ok && gv < g) {
+        // the last V alone, on the barrier of step g (no K)
+        if ((ok = wait_k_stage(g))) {
+          mbar_arrive_expect_tx(&kv_full[g % KS], C::KV_BYTES);
+          ++armed;
+          ok = load_v(&kv_full[g % KS]);
+        }
+      }
       if (*abort_flag) {  // let the loads in flight land before the CTA exits
-        for (int j = g > KS ? g - KS : 0; j < g; ++j) mbar_wait(&k_full[j % KS], (j / KS) & 1, nullptr, nullptr);
-        for (int j = gv > VS ? gv - VS : 0; j < gv; ++j) mbar_wait(&v_full[j % VS], (j / VS) & 1, nullptr, nullptr);
+        for (int j = armed > KS ? armed - KS : 0; j < armed; ++j)
+          mbar_wait(&kv_full[j % KS], (j / KS) & 1, nullptr, nullptr);
       }
     } else if (warp == 1 && lane == 0) {
       // ------------------------------------------------------------ MMA issuer
@@ -343,13 +356,15 @@ __global__ void __launch_bounds__(kThreadsP, 1)
       bool pend_first = false, pend_last = false;
       bool ok = true;
       int pv_issued_tiles = 0;  // non-empty tiles whose first PV was issued (o_empty accounting)
-      auto do_pv = [&]() -> bool {
+      auto do_pv = [&](bool last_pv) -> bool {
         const int i = pend_j, st = i % VS;
         if (pend_first && pv_issued_tiles >= 2 &&
             !mbar_wait(&o_empty[pend_ob], ((pv_issued_tiles >> 1) - 1) & 1, abort_flag, p.err))
           return false;
         if (!mbar_wait(&p_ready[i & 1], (i >> 1) & 1, abort_flag, p.err)) return false;
-        if (!mbar_wait(&v_full[st], (i / VS) & 1, abort_flag, p.err)) return false;
+        // V_i landed with K_i+1 (kv_full of step i+1, waited before S_i+1 was issued), or
+        // alone after the last step
+        if (last_pv && !mbar_wait(&kv_full[(i + 1) % KS], ((i + 1) / KS) & 1, abort_flag, p.err)) return false;
         tc_fence_after();
         const uint32_t p_tmem = tmem + (i & 1) * C::BS;  // P_i lives in the first columns of S buffer i&1
         const uint32_t o_tmem = tmem + C::O_COL0 + pend_ob * D;
@@ -377,7 +392,7 @@ __global__ void __launch_bounds__(kThreadsP, 1)
         const int nsteps = (n + C::SUB - 1) / C::SUB;
         for (int j = 0; j < nsteps; ++j, ++jg) {
           const int st = jg % KS;
-          if (!(ok = mbar_wait(&k_full[st], (jg / KS) & 1, abort_flag, p.err))) break;
+          if (!(ok = mbar_wait(&kv_full[st], (jg / KS) & 1, abort_flag, p.err))) break;
           tc_fence_after();
           const uint32_t d_tmem = tmem + (jg & 1) * C::BS;
 #pragma unroll
@@ -389,7 +404,7 @@ __global__ void __launch_bounds__(kThreadsP, 1)
           }
           tc_commit(&s_full[jg & 1]);
           if (j == nsteps - 1) tc_commit(&q_empty[qb]);
-          if (pend_j >= 0 && !(ok = do_pv())) break;
+          if (pend_j >= 0 && !(ok = do_pv(false))) break;
           pend_j = jg;
           pend_ob = e & 1;
           pend_first = j == 0;
@@ -397,7 +412,7 @@ __global__ void __launch_bounds__(kThreadsP, 1)
         }
         ++e;
       }
-      if (ok && pend_j >= 0) ok = do_pv();
+      if (ok && pend_j >= 0) ok = do_pv(true);
       tc_commit(drain);
       mbar_wait(drain, 0, nullptr, nullptr);
     } else if (warp >= 2) {
