@@ -35,26 +35,53 @@ __device__ __forceinline__ float row_max(const uint32_t (&sr)[BN]) {
   return fmaxf(fmaxf(fmaxf(m[0], m[1]), fmaxf(m[2], m[3])), fmaxf(fmaxf(m[4], m[5]), fmaxf(m[6], m[7])));
 }
 
+// Two fp32 lanes in one 64-bit register, for the paired FP32 instructions of
+// sm_100 (fma.rn.f32x2, add.rn.f32x2): one instruction issue per two values.
+__device__ __forceinline__ uint64_t f32x2_pack(float lo, float hi) {
+  uint64_t r;
+  asm("mov.b64 %0, {%1, %2};" : "=l"(r) : "f"(lo), "f"(hi));
+  return r;
+}
+__device__ __forceinline__ void f32x2_unpack(uint64_t v, float& lo, float& hi) {
+  asm("mov.b64 {%0, %1}, %2;" : "=f"(lo), "=f"(hi) : "l"(v));
+}
+__device__ __forceinline__ uint64_t f32x2_fma(uint64_t a, uint64_t b, uint64_t c) {
+  uint64_t d;
+  asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(d) : "l"(a), "l"(b), "l"(c));
+  return d;
+}
+__device__ __forceinline__ uint64_t f32x2_add(uint64_t a, uint64_t b) {
+  uint64_t d;
+  asm("add.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(a), "l"(b));
+  return d;
+}
+
 // p = 2^(s * scale - m) packed in pairs into pr; returns sum(p) (four
-// independent partial sums).
+// independent partial sums, two paired accumulators).
 template <int BN, bool BF16>
 __device__ __forceinline__ float exp_block(const uint32_t (&sr)[BN], uint32_t (&pr)[BN / 2], float scale_log2,
                                            float neg_m) {
-  float a0 = 0.f, a1 = 0.f, a2 = 0.f, a3 = 0.f;
+  const uint64_t sc2 = f32x2_pack(scale_log2, scale_log2);
+  const uint64_t nm2 = f32x2_pack(neg_m, neg_m);
+  uint64_t a01 = f32x2_pack(0.f, 0.f), a23 = a01;
 #pragma unroll
   for (int i = 0; i < BN / 2; i += 2) {
-    const float p0 = ex2_approx(fmaf(__uint_as_float(sr[2 * i]), scale_log2, neg_m));
-    const float p1 = ex2_approx(fmaf(__uint_as_float(sr[2 * i + 1]), scale_log2, neg_m));
-    const float p2 = ex2_approx(fmaf(__uint_as_float(sr[2 * i + 2]), scale_log2, neg_m));
-    const float p3 = ex2_approx(fmaf(__uint_as_float(sr[2 * i + 3]), scale_log2, neg_m));
-    a0 += p0;
-    a1 += p1;
-    a2 += p2;
-    a3 += p3;
+    const uint64_t x01 = f32x2_fma(f32x2_pack(__uint_as_float(sr[2 * i]), __uint_as_float(sr[2 * i + 1])), sc2, nm2);
+    const uint64_t x23 =
+        f32x2_fma(f32x2_pack(__uint_as_float(sr[2 * i + 2]), __uint_as_float(sr[2 * i + 3])), sc2, nm2);
+    float x0, x1, x2, x3;
+    f32x2_unpack(x01, x0, x1);
+    f32x2_unpack(x23, x2, x3);
+    const float p0 = ex2_approx(x0), p1 = ex2_approx(x1), p2 = ex2_approx(x2), p3 = ex2_approx(x3);
+    a01 = f32x2_add(a01, f32x2_pack(p0, p1));
+    a23 = f32x2_add(a23, f32x2_pack(p2, p3));
     pr[i] = pack2<BF16>(p0, p1);
     pr[i + 1] = pack2<BF16>(p2, p3);
   }
-  return (a0 + a1) + (a2 + a3);
+  float s0, s1, s2, s3;
+  f32x2_unpack(a01, s0, s1);
+  f32x2_unpack(a23, s2, s3);
+  return (s0 + s2) + (s1 + s3);
 }
 
 // One block of the row's online softmax.  sr: raw scores (keys past the end
