@@ -70,6 +70,12 @@ std::atomic<unsigned> g_launches{0};
 constexpr int kTileRing = 8;   // tile numbers in flight between the producer and the other roles
 constexpr int kTileUsers = 11;  // MMA thread + 4 softmax + 4 epilogue + 2 Q-gather warps
 
+// One claimed tile as the producer hands it to the other roles: the tile
+// number (-1 = no more), its plan entries e0 .. e0+n, its (b, h) and tile row.
+struct TileSlot {
+  int w, e0, n, b, h, t, pad0, pad1;
+};
+
 struct TcpParams {
   const int32_t* tile_ptr;
   const int32_t* tile_col;
@@ -127,7 +133,7 @@ struct TcpCfg {
   static constexpr int BOX_BYTES = BN * 128;  // one entry's rows of one 64-column chunk
   static constexpr int Q_BYTES = BM * D * 2;
   static constexpr int KV_BYTES = BS * D * 2;
-  static constexpr int BAR_BYTES = 512;
+  static constexpr int BAR_BYTES = 768;
   static constexpr int STATS_BYTES = 2 * 2 * BM * 4;  // [buffer][m, l][row] fp32
   static constexpr bool fits(int ks, int vs) {
     return 2 * Q_BYTES + (ks + vs) * KV_BYTES + BAR_BYTES + STATS_BYTES <= kSmemLimitP;
@@ -141,7 +147,8 @@ struct TcpCfg {
   static_assert(SMEM <= kSmemLimitP, "shared memory budget");
   static_assert(2 * BS + 2 * D <= 512, "TMEM budget");
   static_assert(SUB * BN == BS && (SUB == 1 || SUB == 2) && (!PAIR || BN == 64), "block size");
-  static_assert((KS + 21 + 2 * kTileRing) * 8 + 8 + 4 * kTileRing <= BAR_BYTES, "barrier area");
+  static constexpr int RING_OFF = ((KS + 21 + 2 * kTileRing) * 8 + 8 + 15) / 16 * 16;
+  static_assert(RING_OFF + kTileRing * static_cast<int>(sizeof(TileSlot)) <= BAR_BYTES, "barrier area");
 };
 
 template <int D, int BN, bool BF16, bool PAIR>
@@ -178,7 +185,8 @@ __global__ void __launch_bounds__(kThreadsP, 1)
   uint64_t* tile_free = tile_ready + kTileRing;  // [kTileRing] all kTileUsers read it
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(tile_free + kTileRing);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
-  volatile int* tile_ring = abort_flag + 1;      // [kTileRing] tile number, -1 = no more
+  // [kTileRing] claimed tiles with their plan range, (b, h) and row
+  volatile TileSlot* tile_ring = reinterpret_cast<volatile TileSlot*>(reinterpret_cast<uint8_t*>(bars) + C::RING_OFF);
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
@@ -230,7 +238,8 @@ __global__ void __launch_bounds__(kThreadsP, 1)
     }
   }
 
-  // tile w -> (entries e0 .. e0+n of the plan, b, h, tile row t)
+  // tile w -> (entries e0 .. e0+n of the plan, b, h, tile row t); the producer
+  // reads it when it claims the tile and passes it on through the ring
   auto tile_info = [&](int w, int& e0, int& n, int& b, int& h, int& t) {
     const int bh = w / p.T;
     const int r = w - bh * p.T;
@@ -241,12 +250,20 @@ __global__ void __launch_bounds__(kThreadsP, 1)
     e0 = p.tile_ptr[s * p.T + t];
     n = p.tile_ptr[s * p.T + t + 1] - e0;
   };
-  // i-th tile of this CTA from the ring (all lanes of the calling warp, or one
-  // thread); -1 when there are no more or a wait failed
-  auto next_tile = [&](int i) -> int {
+  // i-th tile of this CTA from the ring (every calling thread waits and reads
+  // it; w = -1 when there are no more or a wait failed)
+  auto next_tile = [&](int i, int& w, int& e0, int& n, int& b, int& h, int& t) {
     const int ri = i % kTileRing;
-    if (!mbar_wait(&tile_ready[ri], (i / kTileRing) & 1, abort_flag, p.err)) return -1;
-    return tile_ring[ri];
+    if (!mbar_wait(&tile_ready[ri], (i / kTileRing) & 1, abort_flag, p.err)) {
+      w = -1;
+      return;
+    }
+    w = tile_ring[ri].w;
+    e0 = tile_ring[ri].e0;
+    n = tile_ring[ri].n;
+    b = tile_ring[ri].b;
+    h = tile_ring[ri].h;
+    t = tile_ring[ri].t;
   };
 
   if (warp < 4) {
@@ -285,12 +302,17 @@ __global__ void __launch_bounds__(kThreadsP, 1)
         const uint32_t claim = atomicAdd(&g_work_next[p.slot], 1u);
         const int w = claim < static_cast<uint32_t>(p.total_tiles) ? static_cast<int>(claim) : -1;
         const int ri = i % kTileRing;
+        int e0 = 0, n = 0, b = 0, h = 0, t = 0;
+        if (w >= 0) tile_info(w, e0, n, b, h, t);
         if (i >= kTileRing && !(ok = mbar_wait(&tile_free[ri], ((i / kTileRing) - 1) & 1, abort_flag, p.err))) break;
-        tile_ring[ri] = w;
-        mbar_arrive(&tile_ready[ri]);
+        tile_ring[ri].w = w;
+        tile_ring[ri].e0 = e0;
+        tile_ring[ri].n = n;
+        tile_ring[ri].b = b;
+        tile_ring[ri].h = h;
+        tile_ring[ri].t = t;
+        mbar_arrive(&tile_ready[ri]);  // release: the entry is visible to every waiter
         if (w < 0) break;
-        int e0, n, b, h, t;
-        tile_info(w, e0, n, b, h, t);
         if (n == 0) continue;
         const int qb = e & 1;
         if (!p.q_perm) {  // (permuted queries: warps 2-3 gather Q)
@@ -380,11 +402,10 @@ __global__ void __launch_bounds__(kThreadsP, 1)
         return true;
       };
       for (int i = 0; ok; ++i) {
-        const int w = next_tile(i);
-        if (w < 0) break;
-        int e0, n, b, h, t;
-        tile_info(w, e0, n, b, h, t);
+        int w, e0, n, b, h, t;
+        next_tile(i, w, e0, n, b, h, t);
         mbar_arrive(&tile_free[i % kTileRing]);
+        if (w < 0) break;
         if (n == 0) continue;
         const int qb = e & 1;
         if (!(ok = mbar_wait(&q_full[qb], (e >> 1) & 1, abort_flag, p.err))) break;
@@ -423,12 +444,11 @@ __global__ void __launch_bounds__(kThreadsP, 1)
       int e = 0;
       bool ok = true;
       for (int i = 0;; ++i) {
-        const int w = __shfl_sync(0xffffffffu, next_tile(i), 0);
-        if (w < 0) break;
-        int e0, n, b, h, t;
-        tile_info(w, e0, n, b, h, t);
+        int w, e0, n, b, h, t;
+        next_tile(i, w, e0, n, b, h, t);
         __syncwarp();
         if (lane == 0) mbar_arrive(&tile_free[i % kTileRing]);
+        if (w < 0) break;
         if (!p.q_perm || n == 0) continue;
         const int qb = e & 1;
         if (e >= 2)
@@ -471,12 +491,11 @@ __global__ void __launch_bounds__(kThreadsP, 1)
     int e = 0, jg = 0;
     bool ok = true;
     for (int i = 0;; ++i) {
-      const int w = __shfl_sync(0xffffffffu, next_tile(i), 0);
-      if (w < 0) break;
-      int e0, n, b, h, t;
-      tile_info(w, e0, n, b, h, t);
+      int w, e0, n, b, h, t;
+      next_tile(i, w, e0, n, b, h, t);
       __syncwarp();
       if (lane == 0) mbar_arrive(&tile_free[i % kTileRing]);
+      if (w < 0) break;
       if (n == 0) continue;  // the epilogue writes its zero rows
       const int ob = e & 1;
       float m_run = -INFINITY, l_run = 0.f;
@@ -562,12 +581,11 @@ __global__ void __launch_bounds__(kThreadsP, 1)
     int e = 0;
     bool ok = true;
     for (int i = 0;; ++i) {
-      const int w = __shfl_sync(0xffffffffu, next_tile(i), 0);
-      if (w < 0) break;
-      int e0, n, b, h, t;
-      tile_info(w, e0, n, b, h, t);
+      int w, e0, n, b, h, t;
+      next_tile(i, w, e0, n, b, h, t);
       __syncwarp();
       if (lane == 0) mbar_arrive(&tile_free[i % kTileRing]);
+      if (w < 0) break;
       const int grow = t * 128 + row;
       // destination row: the permuted query's original row
       int64_t drow = grow;
