@@ -11,8 +11,8 @@
 // without one), and CTAs claim them from a global counter: longest tiles
 // first within a head, dynamically, so the CTAs finish together, while the
 // CTAs in flight still share a head's K / V in L2.  The producer claims a
-// tile and passes its number to the other roles through a small ring in
-// shared memory.  The counter is one of kWorkSlots per device, taken in turn
+// tile and passes its number, plan range, (b, h) and row to the other roles
+// through a small ring in shared memory.  The counter is one of kWorkSlots per device, taken in turn
 // by successive launches; the last CTA to finish resets it.  Roles:
 //  * warp 0, one thread: TMA producer (Q per tile, then K_g and V_g-1 per
 //    step, V one step behind K because PV_g-1 is issued after S_g; both land
