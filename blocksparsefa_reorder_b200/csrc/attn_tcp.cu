@@ -68,7 +68,11 @@ __device__ uint32_t g_work_done[kWorkSlots];
 std::atomic<unsigned> g_launches{0};
 
 constexpr int kTileRing = 8;   // tile numbers in flight between the producer and the other roles
-constexpr int kTileUsers = 11;  // MMA thread + 4 softmax + 4 epilogue + 2 Q-gather warps
+// readers of each tile-ring entry: MMA thread + 4 softmax + 4 epilogue warps,
+// and the 2 Q-gather warps when there is a query permutation (without one they
+// leave at once rather than poll the ring next to the softmax warps)
+constexpr int kTileUsers = 9;
+constexpr int kTileUsersGather = 11;
 
 // One claimed tile as the producer hands it to the other roles: the tile
 // number (-1 = no more), its plan entries e0 .. e0+n, its (b, h) and tile row.
@@ -207,7 +211,7 @@ __global__ void __launch_bounds__(kThreadsP, 1)
     mbar_init(drain, 1);
     for (int i = 0; i < kTileRing; ++i) {
       mbar_init(&tile_ready[i], 1);
-      mbar_init(&tile_free[i], kTileUsers);
+      mbar_init(&tile_free[i], p.q_perm ? kTileUsersGather : kTileUsers);
     }
     *abort_flag = 0;
     fence_mbar_init();
@@ -436,7 +440,7 @@ __global__ void __launch_bounds__(kThreadsP, 1)
       if (ok && pend_j >= 0) ok = do_pv(true);
       tc_commit(drain);
       mbar_wait(drain, 0, nullptr, nullptr);
-    } else if (warp >= 2) {
+    } else if (warp >= 2 && p.q_perm) {
       // ------------------------------------------------- Q gather (permuted queries)
       // Warp 2 fills rows 0-63 of the tile, warp 3 rows 64-127, each row
       // as 16-byte granules into the 128-byte-swizzled chunks the MMA reads.
