@@ -71,6 +71,7 @@ PROTOS = {
     "bsa_blockmask_from_coords": ([_vp, _vp, _i64, _i64, _i32, _i32, _i32, _vp, _vp, _vp, _vp, _vp], ctypes.c_int),
     "bsa_fwd_reordered_workspace_bytes": ([ctypes.POINTER(FwdArgs), ctypes.POINTER(_sz)], ctypes.c_int),
     "bsa_fwd_reordered": ([ctypes.POINTER(FwdArgs), _vp, _vp, _i32, _vp, _sz, _vp], ctypes.c_int),
+    "bsa_test_arm_wait_timeout": ([ctypes.c_uint32], ctypes.c_int),
 }
 EXPORTED = tuple(PROTOS)
 

@@ -39,11 +39,13 @@ int validate_fwd(const bsa_fwd_args* a) {
   if (!(a->plan.mask_h == 1 || a->plan.mask_h == a->H)) return BSA_ERR_SHAPE;
   if (!(a->sm_scale > 0.f) || !isfinite(a->sm_scale)) return BSA_ERR_UNSUPPORTED;
   if (a->kernel < BSA_KERNEL_AUTO || a->kernel > BSA_KERNEL_TCGEN05) return BSA_ERR_INVALID_ARG;
-  if (static_cast<int64_t>(a->B) * a->H > 65535) return BSA_ERR_UNSUPPORTED;  // grid.y
   return BSA_OK;
 }
 
-bool simt_supported(const bsa_fwd_args* a) { return a->D == 16 || a->D == 32 || a->D == 64 || a->D == 128; }
+// The SIMT kernel's grid has one y index per (b, h).
+bool simt_supported(const bsa_fwd_args* a) {
+  return (a->D == 16 || a->D == 32 || a->D == 64 || a->D == 128) && static_cast<int64_t>(a->B) * a->H <= 65535;
+}
 
 size_t round256(size_t x) { return (x + 255) & ~size_t(255); }
 
@@ -55,13 +57,14 @@ int launch_tc(const bsa_fwd_args* a, cudaStream_t st) { return launch_attn_tcp(a
 bool fused_reorder(const bsa_fwd_args* a) { return a->kernel != BSA_KERNEL_SIMT && attn_tc_supported(a); }
 
 // Workspace layout of bsa_fwd_reordered, 256-byte aligned regions:
-//   [q'] [k' v'] [o' lse'] -- k', v' when kv_perm is given; q', o', lse' when
-//   q_perm is and the forward is not the fused one.
+//   [q'] [k' v'] [o' lse'] [check] -- k', v' when kv_perm is given; q', o',
+//   lse' when q_perm is and the forward is not the fused one; the bits of the
+//   permutation check when an error word is given.
 struct ReorderLayout {
-  size_t q, k, v, o, lse, total;
+  size_t q, k, v, o, lse, check, total;
 };
 
-ReorderLayout reorder_layout(const bsa_fwd_args* a, bool has_q, bool has_kv) {
+ReorderLayout reorder_layout(const bsa_fwd_args* a, bool has_q, bool has_kv, bool check) {
   const size_t tensor = round256(static_cast<size_t>(a->B) * a->H * a->N * a->D * dtype_bytes(a->dtype));
   const size_t lse = round256(static_cast<size_t>(a->B) * a->H * a->N * sizeof(float));
   ReorderLayout L{};
@@ -83,6 +86,10 @@ ReorderLayout reorder_layout(const bsa_fwd_args* a, bool has_q, bool has_kv) {
       L.lse = off;
       off += lse;
     }
+  }
+  if (check) {
+    L.check = off;
+    off += round256(perm_check_bytes(a->N));
   }
   L.total = off;
   return L;
@@ -118,6 +125,11 @@ extern "C" const char* bsa_status_string(int status) {
   }
 }
 
+extern "C" int bsa_test_arm_wait_timeout(uint32_t wait_us) {
+  if (wait_us < 100 || wait_us > 2000000) return BSA_ERR_INVALID_ARG;
+  return arm_test_wait_timeout(wait_us);
+}
+
 extern "C" int bsa_device_supported(int device, int* supported) {
   if (!supported) return BSA_ERR_INVALID_ARG;
   int major = 0, minor = 0;
@@ -150,7 +162,7 @@ extern "C" int bsa_fwd_reordered_workspace_bytes(const bsa_fwd_args* a, size_t* 
   if (!a || !bytes) return BSA_ERR_INVALID_ARG;
   const int rc = validate_fwd(a);
   if (rc) return rc;
-  *bytes = reorder_layout(a, !fused_reorder(a), true).total;
+  *bytes = reorder_layout(a, !fused_reorder(a), true, a->err_flag != nullptr).total;
   return BSA_OK;
 }
 
@@ -160,13 +172,24 @@ extern "C" int bsa_fwd_reordered(const bsa_fwd_args* a, const void* q_perm, cons
   if (rc) return rc;
   if ((q_perm || kv_perm) && perm_dtype != BSA_INDEX_I32 && perm_dtype != BSA_INDEX_I64) return BSA_ERR_DTYPE;
   const bool fused = fused_reorder(a);
-  const ReorderLayout L = reorder_layout(a, !fused && q_perm != nullptr, kv_perm != nullptr);
+  const bool check = a->err_flag && (q_perm || kv_perm);
+  const ReorderLayout L = reorder_layout(a, !fused && q_perm != nullptr, kv_perm != nullptr, check);
   if (L.total && (!workspace || workspace_bytes < L.total)) return BSA_ERR_WORKSPACE;
   if ((rc = check_device())) return rc;
   cudaStream_t st = static_cast<cudaStream_t>(stream);
   uint8_t* ws = static_cast<uint8_t*>(workspace);
   const int eb = dtype_bytes(a->dtype);
   bsa_fwd_args inner = *a;
+  // With an error word, both permutations are checked first (range and
+  // repeated values): a repeated q_perm value would make two rows write one
+  // output row, which neither the fused gather / scatter nor the row-copy
+  // kernels can see.
+  if (check) {
+    if (q_perm && (rc = launch_perm_check(q_perm, perm_dtype, a->N, ws + L.check, a->err_flag, st))) return rc;
+    if (kv_perm && kv_perm != q_perm &&
+        (rc = launch_perm_check(kv_perm, perm_dtype, a->N, ws + L.check, a->err_flag, st)))
+      return rc;
+  }
   if (fused) {
     if (kv_perm) {
       inner.k = contiguous(ws + L.k, a);

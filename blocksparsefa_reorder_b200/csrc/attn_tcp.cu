@@ -66,6 +66,8 @@ __device__ uint32_t g_work_next[kWorkSlots];
 __device__ uint32_t g_work_done[kWorkSlots];
 // Launch counter shared by every instantiation of the kernel (they share the slots).
 std::atomic<unsigned> g_launches{0};
+// Armed by bsa_test_arm_wait_timeout: the wait limit (us) of the next forward.
+std::atomic<uint32_t> g_test_wait_us{0};
 
 constexpr int kTileRing = 8;   // tile numbers in flight between the producer and the other roles
 // readers of each tile-ring entry: MMA thread + 4 softmax + 4 epilogue warps,
@@ -98,6 +100,12 @@ struct TcpParams {
   // 0: run.  1 / 2: run only if the plan averages at least / fewer than
   // kPairMinEntries kept blocks per tile (the two forms launched for BLOCK 64).
   int select;
+  // limit of every bounded wait (kWaitNs unless a test shortened it)
+  uint64_t wait_ns;
+  // test of the timeout path: softmax warp 0 of CTA 0 withholds its arrival on
+  // p_ready for the CTA's first step, so the MMA issuer's wait for that step
+  // runs out (no TMA load or MMA is ever counted on that barrier)
+  int withhold_arrive;
 };
 
 // BLOCK 64: tiles averaging at least this many kept key blocks run the form
@@ -258,7 +266,7 @@ __global__ void __launch_bounds__(kThreadsP, 1)
   // it; w = -1 when there are no more or a wait failed)
   auto next_tile = [&](int i, int& w, int& e0, int& n, int& b, int& h, int& t) {
     const int ri = i % kTileRing;
-    if (!mbar_wait(&tile_ready[ri], (i / kTileRing) & 1, abort_flag, p.err)) {
+    if (!mbar_wait(&tile_ready[ri], (i / kTileRing) & 1, abort_flag, p.err, p.wait_ns)) {
       w = -1;
       return;
     }
@@ -281,25 +289,27 @@ __global__ void __launch_bounds__(kThreadsP, 1)
       int pv_b = 0, pv_h = 0;    // the step whose V is still to load (gv < g)
       int pv_kb[C::SUB] = {};
       bool ok = true;
-      int armed = 0;  // kv_full phases armed so far (one per step, one more for the last V)
+      int armed = 0;   // kv_full phases armed so far (one per step, one more for the last V)
+      int qarmed = 0;  // Q tiles loaded by TMA so far
       // the barrier of step gs's K may be re-armed once S_gs-KS completed: the commit
       // after PV_gs-KS-1 (S_0 and S_1 both under the one after PV_0)
       auto wait_k_stage = [&](int gs) -> bool {
         const int sd = gs - KS - 1 > 0 ? gs - KS - 1 : 0;
-        return gs < KS || mbar_wait(&step_done[sd & 3], (sd >> 2) & 1, abort_flag, p.err);
+        return gs < KS || mbar_wait(&step_done[sd & 3], (sd >> 2) & 1, abort_flag, p.err, p.wait_ns);
+      };
+      // V_gv's stage is free once PV_gv-VS completed
+      auto wait_v_stage = [&]() -> bool {
+        return gv < VS || mbar_wait(&step_done[(gv - VS) & 3], ((gv - VS) >> 2) & 1, abort_flag, p.err, p.wait_ns);
       };
       // V_gv into its stage, counted on the barrier of the step it travels with (bar)
-      auto load_v = [&](uint64_t* bar) -> bool {
+      auto load_v = [&](uint64_t* bar) {
         const int st = gv % VS;
-        // V_gv-VS's stage is free once PV_gv-VS completed
-        if (gv >= VS && !mbar_wait(&step_done[(gv - VS) & 3], ((gv - VS) >> 2) & 1, abort_flag, p.err)) return false;
 #pragma unroll
         for (int u = 0; u < C::SUB; ++u)
           for (int c = 0; c < C::NCHUNK; ++c)
             tma_load_4d(sV + st * C::KV_BYTES + c * C::KV_CHUNK + u * C::BOX_BYTES, &tmV, bar, c * 64,
                         pv_kb[u] * BN, pv_h, pv_b);
         ++gv;
-        return true;
       };
       for (int i = 0; ok; ++i) {
         // claim the next tile and pass its number on
@@ -308,7 +318,7 @@ __global__ void __launch_bounds__(kThreadsP, 1)
         const int ri = i % kTileRing;
         int e0 = 0, n = 0, b = 0, h = 0, t = 0;
         if (w >= 0) tile_info(w, e0, n, b, h, t);
-        if (i >= kTileRing && !(ok = mbar_wait(&tile_free[ri], ((i / kTileRing) - 1) & 1, abort_flag, p.err))) break;
+        if (i >= kTileRing && !(ok = mbar_wait(&tile_free[ri], ((i / kTileRing) - 1) & 1, abort_flag, p.err, p.wait_ns))) break;
         tile_ring[ri].w = w;
         tile_ring[ri].e0 = e0;
         tile_ring[ri].n = n;
@@ -320,8 +330,9 @@ __global__ void __launch_bounds__(kThreadsP, 1)
         if (n == 0) continue;
         const int qb = e & 1;
         if (!p.q_perm) {  // (permuted queries: warps 2-3 gather Q)
-          if (e >= 2 && !(ok = mbar_wait(&q_empty[qb], ((e >> 1) - 1) & 1, abort_flag, p.err))) break;
+          if (e >= 2 && !(ok = mbar_wait(&q_empty[qb], ((e >> 1) - 1) & 1, abort_flag, p.err, p.wait_ns))) break;
           mbar_arrive_expect_tx(&q_full[qb], C::Q_BYTES);
+          ++qarmed;
           for (int c = 0; c < C::NCHUNK; ++c)
             tma_load_4d(sQ + qb * C::Q_BYTES + c * C::Q_CHUNK, &tmQ, &q_full[qb], c * 64, t * 128, h, b);
         }
@@ -341,15 +352,23 @@ __global__ void __launch_bounds__(kThreadsP, 1)
               kb[u] = 0;
             }
           }
-          // K_g and (from the second step on) V_g-1 complete one phase of kv_full[st]
-          mbar_arrive_expect_tx(&kv_full[st], gv < g ? 2 * C::KV_BYTES : C::KV_BYTES);
+          // K_g and (from the second step on) V_g-1 complete one phase of
+          // kv_full[st]: each load's bytes are announced before it is issued
+          // and the phase's one arrival comes last, so a V stage that never
+          // frees (a role gave up) leaves a phase that completes with K alone
           ++armed;
+          mbar_expect_tx(&kv_full[st], C::KV_BYTES);
 #pragma unroll
           for (int u = 0; u < C::SUB; ++u)
             for (int c = 0; c < C::NCHUNK; ++c)
               tma_load_4d(sK + st * C::KV_BYTES + c * C::KV_CHUNK + u * C::BOX_BYTES, &tmK, &kv_full[st], c * 64,
                           kb[u] * BN, h, b);
-          if (gv < g && !(ok = load_v(&kv_full[st]))) break;
+          if (gv < g && (ok = wait_v_stage())) {
+            mbar_expect_tx(&kv_full[st], C::KV_BYTES);
+            load_v(&kv_full[st]);
+          }
+          mbar_arrive(&kv_full[st]);
+          if (!ok) break;
           pv_b = b;
           pv_h = h;
 #pragma unroll
@@ -358,16 +377,20 @@ __global__ void __launch_bounds__(kThreadsP, 1)
       }
       if (ok && gv < g) {
         // the last V alone, on the barrier of step g (no K)
-        if ((ok = wait_k_stage(g))) {
-          mbar_arrive_expect_tx(&kv_full[g % KS], C::KV_BYTES);
+        if ((ok = wait_k_stage(g) && wait_v_stage())) {
           ++armed;
-          ok = load_v(&kv_full[g % KS]);
+          mbar_arrive_expect_tx(&kv_full[g % KS], C::KV_BYTES);
+          load_v(&kv_full[g % KS]);
         }
       }
-      if (*abort_flag) {  // let the loads in flight land before the CTA exits
-        for (int j = armed > KS ? armed - KS : 0; j < armed; ++j)
-          mbar_wait(&kv_full[j % KS], (j / KS) & 1, nullptr, nullptr);
-      }
+      // Every load this thread issued lands before the CTA exits, also when a
+      // role gave up and the loads were never consumed: the last phase armed on
+      // each K/V barrier and on each Q barrier (all earlier phases completed
+      // before their barrier was re-armed).
+      for (int j = armed > KS ? armed - KS : 0; j < armed; ++j)
+        mbar_wait(&kv_full[j % KS], (j / KS) & 1, nullptr, nullptr, p.wait_ns);
+      for (int j = qarmed > 2 ? qarmed - 2 : 0; j < qarmed; ++j)
+        mbar_wait(&q_full[j & 1], (j >> 1) & 1, nullptr, nullptr, p.wait_ns);
     } else if (warp == 1 && lane == 0) {
       // ------------------------------------------------------------ MMA issuer
       constexpr uint32_t idesc_qk = make_idesc_f16(BF16, 128, C::BS, false, false);
@@ -385,12 +408,12 @@ __global__ void __launch_bounds__(kThreadsP, 1)
       auto do_pv = [&](bool last_pv) -> bool {
         const int i = pend_j, st = i % VS;
         if (pend_first && pv_issued_tiles >= 2 &&
-            !mbar_wait(&o_empty[pend_ob], ((pv_issued_tiles >> 1) - 1) & 1, abort_flag, p.err))
+            !mbar_wait(&o_empty[pend_ob], ((pv_issued_tiles >> 1) - 1) & 1, abort_flag, p.err, p.wait_ns))
           return false;
-        if (!mbar_wait(&p_ready[i & 1], (i >> 1) & 1, abort_flag, p.err)) return false;
+        if (!mbar_wait(&p_ready[i & 1], (i >> 1) & 1, abort_flag, p.err, p.wait_ns)) return false;
         // V_i landed with K_i+1 (kv_full of step i+1, waited before S_i+1 was issued), or
         // alone after the last step
-        if (last_pv && !mbar_wait(&kv_full[(i + 1) % KS], ((i + 1) / KS) & 1, abort_flag, p.err)) return false;
+        if (last_pv && !mbar_wait(&kv_full[(i + 1) % KS], ((i + 1) / KS) & 1, abort_flag, p.err, p.wait_ns)) return false;
         tc_fence_after();
         const uint32_t p_tmem = tmem + (i & 1) * C::BS;  // P_i lives in the first columns of S buffer i&1
         const uint32_t o_tmem = tmem + C::O_COL0 + pend_ob * D;
@@ -412,12 +435,12 @@ __global__ void __launch_bounds__(kThreadsP, 1)
         if (w < 0) break;
         if (n == 0) continue;
         const int qb = e & 1;
-        if (!(ok = mbar_wait(&q_full[qb], (e >> 1) & 1, abort_flag, p.err))) break;
+        if (!(ok = mbar_wait(&q_full[qb], (e >> 1) & 1, abort_flag, p.err, p.wait_ns))) break;
         tc_fence_after();
         const int nsteps = (n + C::SUB - 1) / C::SUB;
         for (int j = 0; j < nsteps; ++j, ++jg) {
           const int st = jg % KS;
-          if (!(ok = mbar_wait(&kv_full[st], (jg / KS) & 1, abort_flag, p.err))) break;
+          if (!(ok = mbar_wait(&kv_full[st], (jg / KS) & 1, abort_flag, p.err, p.wait_ns))) break;
           tc_fence_after();
           const uint32_t d_tmem = tmem + (jg & 1) * C::BS;
 #pragma unroll
@@ -439,7 +462,7 @@ __global__ void __launch_bounds__(kThreadsP, 1)
       }
       if (ok && pend_j >= 0) ok = do_pv(true);
       tc_commit(drain);
-      mbar_wait(drain, 0, nullptr, nullptr);
+      mbar_wait(drain, 0, nullptr, nullptr, p.wait_ns);
     } else if (warp >= 2 && p.q_perm) {
       // ------------------------------------------------- Q gather (permuted queries)
       // Warp 2 fills rows 0-63 of the tile, warp 3 rows 64-127, each row
@@ -456,7 +479,7 @@ __global__ void __launch_bounds__(kThreadsP, 1)
         if (!p.q_perm || n == 0) continue;
         const int qb = e & 1;
         if (e >= 2)
-          ok = ok && __all_sync(0xffffffffu, mbar_wait(&q_empty[qb], ((e >> 1) - 1) & 1, abort_flag, p.err));
+          ok = ok && __all_sync(0xffffffffu, mbar_wait(&q_empty[qb], ((e >> 1) - 1) & 1, abort_flag, p.err, p.wait_ns));
         ++e;
         if (!ok) continue;
         for (int k = 0; k < 2; ++k) {
@@ -507,7 +530,7 @@ __global__ void __launch_bounds__(kThreadsP, 1)
       for (int j = 0; j < nsteps; ++j, ++jg) {
         const int sb = jg & 1;
         // after a failed wait every later wait returns at once (abort flag)
-        if (!(ok = ok && __all_sync(0xffffffffu, mbar_wait(&s_full[sb], (jg >> 1) & 1, abort_flag, p.err))))
+        if (!(ok = ok && __all_sync(0xffffffffu, mbar_wait(&s_full[sb], (jg >> 1) & 1, abort_flag, p.err, p.wait_ns))))
           continue;
         tc_fence_after();
         uint32_t sr[C::BS];
@@ -542,7 +565,7 @@ __global__ void __launch_bounds__(kThreadsP, 1)
           if (__any_sync(0xffffffffu, alpha != 1.f)) {
             // O holds the sum up to block j-1 of this tile: wait for that PV, rescale in TMEM.
             if (!(ok = __all_sync(0xffffffffu,
-                                  mbar_wait(&step_done[(jg - 1) & 3], ((jg - 1) >> 2) & 1, abort_flag, p.err))))
+                                  mbar_wait(&step_done[(jg - 1) & 3], ((jg - 1) >> 2) & 1, abort_flag, p.err, p.wait_ns))))
               continue;
             tc_fence_after();
 #pragma unroll
@@ -565,11 +588,11 @@ __global__ void __launch_bounds__(kThreadsP, 1)
         tmem_wait_st();
         tc_fence_before();
         __syncwarp();
-        if (lane == 0) mbar_arrive(&p_ready[sb]);
+        if (lane == 0 && !(p.withhold_arrive && jg == 0 && q4 == 0 && blockIdx.x == 0)) mbar_arrive(&p_ready[sb]);
       }
       // hand the row's (m, l) to the epilogue warps
       if (e >= 2)
-        ok = ok && __all_sync(0xffffffffu, mbar_wait(&stats_empty[ob], ((e >> 1) - 1) & 1, abort_flag, p.err));
+        ok = ok && __all_sync(0xffffffffu, mbar_wait(&stats_empty[ob], ((e >> 1) - 1) & 1, abort_flag, p.err, p.wait_ns));
       stats[ob * 256 + row] = m_run;
       stats[ob * 256 + 128 + row] = l_run;
       __syncwarp();
@@ -613,7 +636,7 @@ __global__ void __launch_bounds__(kThreadsP, 1)
         continue;
       }
       const int ob = e & 1;
-      ok = ok && __all_sync(0xffffffffu, mbar_wait(&stats_ready[ob], (e >> 1) & 1, abort_flag, p.err));
+      ok = ok && __all_sync(0xffffffffu, mbar_wait(&stats_ready[ob], (e >> 1) & 1, abort_flag, p.err, p.wait_ns));
       float m_run = 0.f, l_run = 0.f;
       if (ok) {
         m_run = stats[ob * 256 + row];
@@ -621,7 +644,7 @@ __global__ void __launch_bounds__(kThreadsP, 1)
       }
       __syncwarp();
       if (lane == 0) mbar_arrive(&stats_empty[ob]);
-      ok = ok && __all_sync(0xffffffffu, mbar_wait(&o_final[ob], (e >> 1) & 1, abort_flag, p.err));
+      ok = ok && __all_sync(0xffffffffu, mbar_wait(&o_final[ob], (e >> 1) & 1, abort_flag, p.err, p.wait_ns));
       if (ok) {
         tc_fence_after();
         const float inv_l = l_run > 0.f ? 1.f / l_run : 0.f;
@@ -682,24 +705,86 @@ int sm_count() {
   return count[dev];
 }
 
+// The three tensor maps of a forward, encoded once per argument set: the
+// encoding is host work that every call with the same tensors would repeat.
+// A small per-thread cache keyed by everything the encoding reads.
+struct MapKey {
+  const void* q;
+  const void* k;
+  const void* v;
+  int64_t s[9];
+  int B, H, N, D, bf16, bn;
+  bool operator==(const MapKey& o) const {
+    if (q != o.q || k != o.k || v != o.v || B != o.B || H != o.H || N != o.N || D != o.D || bf16 != o.bf16 ||
+        bn != o.bn)
+      return false;
+    for (int i = 0; i < 9; ++i)
+      if (s[i] != o.s[i]) return false;
+    return true;
+  }
+};
+struct MapEntry {
+  MapKey key;
+  CUtensorMap mq, mk, mv;
+  bool used;
+};
+constexpr int kMapCache = 8;
+
+int tensor_maps(const bsa_fwd_args* a, int D, bool bf16, int bn, CUtensorMap* mq, CUtensorMap* mk, CUtensorMap* mv) {
+  thread_local MapEntry cache[kMapCache] = {};
+  thread_local int next = 0;
+  MapKey key{a->q.data, a->k.data, a->v.data,
+             {a->q.stride_b, a->q.stride_h, a->q.stride_n, a->k.stride_b, a->k.stride_h, a->k.stride_n, a->v.stride_b,
+              a->v.stride_h, a->v.stride_n},
+             a->B, a->H, a->N, D, bf16 ? 1 : 0, bn};
+  for (int i = 0; i < kMapCache; ++i) {
+    if (cache[i].used && cache[i].key == key) {
+      *mq = cache[i].mq;
+      *mk = cache[i].mk;
+      *mv = cache[i].mv;
+      return BSA_OK;
+    }
+  }
+  int r;
+  if ((r = make_tensor_map_4d(mq, a->q, a->B, a->H, a->N, D, bf16, 128))) return r;
+  if ((r = make_tensor_map_4d(mk, a->k, a->B, a->H, a->N, D, bf16, bn))) return r;
+  if ((r = make_tensor_map_4d(mv, a->v, a->B, a->H, a->N, D, bf16, bn))) return r;
+  MapEntry& e = cache[next];
+  next = (next + 1) % kMapCache;
+  e.key = key;
+  e.mq = *mq;
+  e.mk = *mk;
+  e.mv = *mv;
+  e.used = true;
+  return BSA_OK;
+}
+
 template <int D, int BN, bool BF16, bool PAIR>
-int launch_p(const bsa_fwd_args* a, cudaStream_t st, const void* q_perm, int perm_dtype, int select) {
+int launch_p(const bsa_fwd_args* a, cudaStream_t st, const void* q_perm, int perm_dtype, int select,
+             uint32_t test_wait_us) {
   using C = TcpCfg<D, BN, PAIR>;
   auto kern = attn_tcp_kernel<D, BN, BF16, PAIR>;
   // The setmaxnreg split needs the launch to hold at least the sum of the
   // three warpgroups' shares; with fewer the increase would never be granted.
-  static int checked = 0;  // 1 ok, 2 too few registers
-  if (!checked) {
+  static std::atomic<int> checked{0};  // 1 ok, 2 too few registers
+  if (!checked.load(std::memory_order_relaxed)) {
     cudaFuncAttributes fa;
     BSA_CUDA_CHECK(cudaFuncGetAttributes(&fa, kern));
-    checked = fa.numRegs * kThreadsP >= 128 * (kRegsIssueP + kRegsSoftmaxP + kRegsEpilogueP) ? 1 : 2;
+    checked.store(fa.numRegs * kThreadsP >= 128 * (kRegsIssueP + kRegsSoftmaxP + kRegsEpilogueP) ? 1 : 2);
   }
-  if (checked != 1) return BSA_ERR_UNSUPPORTED;
+  if (checked.load(std::memory_order_relaxed) != 1) return BSA_ERR_UNSUPPORTED;
+  // the shared-memory opt-in, once per device
+  static std::atomic<bool> smem_set[64] = {};
+  int dev = 0;
+  BSA_CUDA_CHECK(cudaGetDevice(&dev));
+  if (dev < 0 || dev >= 64) return BSA_ERR_DEVICE;
+  if (!smem_set[dev].load(std::memory_order_acquire)) {
+    BSA_CUDA_CHECK(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM));
+    smem_set[dev].store(true, std::memory_order_release);
+  }
   CUtensorMap mq, mk, mv;
   int r;
-  if ((r = make_tensor_map_4d(&mq, a->q, a->B, a->H, a->N, D, BF16, 128))) return r;
-  if ((r = make_tensor_map_4d(&mk, a->k, a->B, a->H, a->N, D, BF16, BN))) return r;
-  if ((r = make_tensor_map_4d(&mv, a->v, a->B, a->H, a->N, D, BF16, BN))) return r;
+  if ((r = tensor_maps(a, D, BF16, BN, &mq, &mk, &mv))) return r;
   TcpParams p;
   p.tile_ptr = a->plan.tile_ptr;
   p.tile_col = a->plan.tile_col;
@@ -725,8 +810,9 @@ int launch_p(const bsa_fwd_args* a, cudaStream_t st, const void* q_perm, int per
   p.total_tiles = a->B * a->H * p.T;
   p.scale_log2 = a->sm_scale * 1.4426950408889634f;
   p.select = select;
+  p.wait_ns = test_wait_us ? static_cast<uint64_t>(test_wait_us) * 1000ull : kWaitNs;
+  p.withhold_arrive = test_wait_us ? 1 : 0;
   p.slot = static_cast<int>(g_launches.fetch_add(1, std::memory_order_relaxed) % kWorkSlots);
-  BSA_CUDA_CHECK(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM));
   int grid = sm_count();
   if (grid > p.total_tiles) grid = p.total_tiles;
   // programmatic stream serialization: the CTAs may start (barriers, TMEM)
@@ -751,19 +837,21 @@ int launch_p(const bsa_fwd_args* a, cudaStream_t st, const void* q_perm, int per
 int launch_attn_tcp(const bsa_fwd_args* a, cudaStream_t st, const void* q_perm, int perm_dtype) {
   const bool bf16 = a->dtype == BSA_DTYPE_BF16;
   const int bn = a->plan.block;
+  // an armed timeout test applies to this forward (both BLOCK 64 launches)
+  const uint32_t tw = g_test_wait_us.load(std::memory_order_relaxed) ? g_test_wait_us.exchange(0) : 0u;
   // BLOCK 64: both forms are launched back to back and the plan's density
   // (read on the device, no host synchronisation) picks the one that runs.
 #define BSA_TCP_CASE(D_, BN_)                                                                     \
   if (a->D == D_ && bn == BN_) {                                                                  \
     if constexpr (BN_ == 128)                                                                     \
-      return bf16 ? launch_p<D_, BN_, true, false>(a, st, q_perm, perm_dtype, 0)                  \
-                  : launch_p<D_, BN_, false, false>(a, st, q_perm, perm_dtype, 0);                \
+      return bf16 ? launch_p<D_, BN_, true, false>(a, st, q_perm, perm_dtype, 0, tw)                  \
+                  : launch_p<D_, BN_, false, false>(a, st, q_perm, perm_dtype, 0, tw);                \
     else {                                                                                        \
-      int r_ = bf16 ? launch_p<D_, BN_, true, true>(a, st, q_perm, perm_dtype, 1)                 \
-                    : launch_p<D_, BN_, false, true>(a, st, q_perm, perm_dtype, 1);               \
+      int r_ = bf16 ? launch_p<D_, BN_, true, true>(a, st, q_perm, perm_dtype, 1, tw)                 \
+                    : launch_p<D_, BN_, false, true>(a, st, q_perm, perm_dtype, 1, tw);               \
       if (r_) return r_;                                                                          \
-      return bf16 ? launch_p<D_, BN_, true, false>(a, st, q_perm, perm_dtype, 2)                  \
-                  : launch_p<D_, BN_, false, false>(a, st, q_perm, perm_dtype, 2);                \
+      return bf16 ? launch_p<D_, BN_, true, false>(a, st, q_perm, perm_dtype, 2, tw)                  \
+                  : launch_p<D_, BN_, false, false>(a, st, q_perm, perm_dtype, 2, tw);                \
     }                                                                                             \
   }
   BSA_TCP_CASE(64, 64)
@@ -772,6 +860,11 @@ int launch_attn_tcp(const bsa_fwd_args* a, cudaStream_t st, const void* q_perm, 
   BSA_TCP_CASE(128, 128)
 #undef BSA_TCP_CASE
   return BSA_ERR_UNSUPPORTED;
+}
+
+int arm_test_wait_timeout(uint32_t wait_us) {
+  g_test_wait_us.store(wait_us);
+  return BSA_OK;
 }
 
 }  // namespace bsa

@@ -64,6 +64,11 @@ __device__ __forceinline__ void mbar_arrive_expect_tx(uint64_t* bar, uint32_t by
                : "memory");
 }
 
+// Announce `bytes` more transaction bytes for the current phase without arriving.
+__device__ __forceinline__ void mbar_expect_tx(uint64_t* bar, uint32_t bytes) {
+  asm volatile("mbarrier.expect_tx.relaxed.cta.shared::cta.b64 [%0], %1;" ::"r"(smem_u32(bar)), "r"(bytes) : "memory");
+}
+
 __device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
   uint32_t ok;
   asm volatile(
@@ -82,20 +87,22 @@ __device__ __forceinline__ uint64_t globaltimer_ns() {
   return t;
 }
 
-// Bounded wait on the phase with the given parity.  After kWaitNs of
-// unsuccessful tries (no legitimate wait in these kernels comes close) the
-// wait gives up, ORs BSA_DEVERR_TIMEOUT into the error word, raises the CTA's
-// abort flag and returns false; a raised abort flag (another role of the CTA
-// gave up) also ends the wait.  Callers then skip the rest of their work.
+// Bounded wait on the phase with the given parity.  After limit_ns (default
+// kWaitNs) of unsuccessful tries -- no legitimate wait in these kernels comes
+// close -- the wait gives up, ORs BSA_DEVERR_TIMEOUT into the error word,
+// raises the CTA's abort flag and returns false; a raised abort flag (another
+// role of the CTA gave up) also ends the wait.  Callers then skip the rest of
+// their work.
 constexpr uint64_t kWaitNs = 2000000000ull;
 
-__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, volatile int* abort_flag, int32_t* err) {
+__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, volatile int* abort_flag, int32_t* err,
+                                          uint64_t limit_ns = kWaitNs) {
   if (mbar_try_wait(bar, parity)) return true;
   const uint64_t t0 = globaltimer_ns();
   while (true) {
     if (mbar_try_wait(bar, parity)) return true;
     if (abort_flag && *abort_flag) return false;
-    if (globaltimer_ns() - t0 > kWaitNs) break;
+    if (globaltimer_ns() - t0 > limit_ns) break;
   }
   if (abort_flag) *abort_flag = 1;
   set_err(err, BSA_DEVERR_TIMEOUT);

@@ -23,6 +23,10 @@ int launch_plan_count(const uint8_t* mask, int64_t sb, int64_t sh, int64_t srow,
 int launch_plan_scan(const int32_t* counts, int64_t n, int32_t* tile_ptr, cudaStream_t st);
 int launch_plan_fill(const uint8_t* mask, int64_t sb, int64_t sh, int64_t srow, int mask_b, int mask_h, int nb,
                      int block, const int32_t* tile_ptr, int32_t* tile_col, cudaStream_t st);
+// Bits of a permutation check (ceil(n / 32) words) and the check itself:
+// zeroes `scratch`, then sets BSA_DEVERR_PERM_RANGE / _DUP in `err`.
+size_t perm_check_bytes(int64_t n);
+int launch_perm_check(const void* perm, int perm_dtype, int64_t n, void* scratch, int32_t* err, cudaStream_t st);
 int launch_permute_rows(bsa_tensor4d dst, bsa_tensor4d src, int B, int H, int N, int row_elems, int elt_bytes,
                         const void* perm, int perm_dtype, int inverse, int32_t* err, cudaStream_t st);
 
@@ -40,6 +44,9 @@ int make_tensor_map_4d(CUtensorMap* m, const bsa_tensor4d& t, int B, int H, int 
 // scatter O / lse rows to q_perm[row] inside the kernel.
 int launch_attn_tcp(const bsa_fwd_args* a, cudaStream_t st, const void* q_perm = nullptr,
                     int perm_dtype = BSA_INDEX_I64);
+// Arms the timeout test for the next launch_attn_tcp call (see
+// bsa_test_arm_wait_timeout).
+int arm_test_wait_timeout(uint32_t wait_us);
 
 
 }  // namespace bsa

@@ -344,6 +344,23 @@ __global__ void inverse_perm_kernel(const void* __restrict__ perm, int perm_dtyp
   }
 }
 
+// Permutation check with a bit per value: values outside [0, n) set
+// BSA_DEVERR_PERM_RANGE, a value seen twice sets BSA_DEVERR_PERM_DUP.
+// `seen` holds ceil(n / 32) words, zeroed beforehand.
+__global__ void perm_check_kernel(const void* __restrict__ perm, int perm_dtype, int64_t n,
+                                  uint32_t* __restrict__ seen, int32_t* err) {
+  for (int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; i < n;
+       i += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+    const int64_t p = load_index(perm, perm_dtype, i);
+    if (p < 0 || p >= n) {
+      set_err(err, BSA_DEVERR_PERM_RANGE);
+      continue;
+    }
+    const uint32_t bit = 1u << (p & 31);
+    if (atomicOr(seen + (p >> 5), bit) & bit) set_err(err, BSA_DEVERR_PERM_DUP);
+  }
+}
+
 __global__ void remap_kernel(const int64_t* __restrict__ idx, int64_t count, const int64_t* __restrict__ inv,
                              int64_t n, int64_t* __restrict__ out, int32_t* err) {
   for (int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; i < count;
@@ -456,6 +473,14 @@ int launch_permute_rows(bsa_tensor4d dst, bsa_tensor4d src, int B, int H, int N,
     default: BSA_PERM_LAUNCH(2); break;
   }
 #undef BSA_PERM_LAUNCH
+  return cudaGetLastError() == cudaSuccess ? BSA_OK : BSA_ERR_CUDA;
+}
+
+size_t perm_check_bytes(int64_t n) { return static_cast<size_t>((n + 31) / 32) * 4; }
+
+int launch_perm_check(const void* perm, int perm_dtype, int64_t n, void* scratch, int32_t* err, cudaStream_t st) {
+  BSA_CUDA_CHECK(cudaMemsetAsync(scratch, 0, perm_check_bytes(n), st));
+  perm_check_kernel<<<grid_for(n, 256), 256, 0, st>>>(perm, perm_dtype, n, static_cast<uint32_t*>(scratch), err);
   return cudaGetLastError() == cudaSuccess ? BSA_OK : BSA_ERR_CUDA;
 }
 

@@ -193,14 +193,32 @@ BSA_API int bsa_blockmask_from_coords(const int64_t* rows, const int64_t* cols, 
                                       const int64_t* col_inv, uint8_t* mask_out, int32_t* err_flag,
                                       void* stream);
 
-/* "With reordering" forward, unfused: gather q by q_perm and k, v by kv_perm
- * into the workspace, run bsa_fwd with the mask in the new order, scatter o
- * (and lse) back by q_perm.  Either permutation may be NULL (identity).
- * Mirrors the timed loop of BlockSparseTriton_Naive.py:129-161.  `args->o`
- * and `args->lse` receive results in ORIGINAL order. */
+/* "With reordering" forward: q rows taken through q_perm, k / v rows
+ * through kv_perm, attention with the mask in the new order, o (and lse)
+ * rows returned through q_perm to the ORIGINAL order.  Either permutation may
+ * be NULL (identity).  Mirrors the timed loop of
+ * BlockSparseTriton_Naive.py:129-161 and the fused kernel
+ * triton_kernels/BlockSparse_Fused.py:115-223.  On the tcgen05 path the
+ * query gather and the o / lse scatter run inside the attention kernel and
+ * k, v are permuted into the workspace; the SIMT path permutes every tensor.
+ * With `args->err_flag` set, both permutations are first checked on the
+ * device (values outside [0, N) set BSA_DEVERR_PERM_RANGE, repeated values
+ * BSA_DEVERR_PERM_DUP); the workspace then also holds the check's bits, so
+ * query the size with the same args. */
 BSA_API int bsa_fwd_reordered_workspace_bytes(const bsa_fwd_args* args, size_t* bytes);
 BSA_API int bsa_fwd_reordered(const bsa_fwd_args* args, const void* q_perm, const void* kv_perm,
                               int32_t perm_dtype, void* workspace, size_t workspace_bytes, void* stream);
+
+/* Test hook for the bounded device waits, not for production use.  Arms the
+ * NEXT tcgen05 forward (bsa_fwd / bsa_fwd_reordered) of the process: every
+ * mbarrier wait of its launch gives up after `wait_us` microseconds (100 ..
+ * 2,000,000) instead of 2 s, and one softmax warp of CTA 0 withholds its
+ * arrival for that CTA's first step, so the MMA issuer's wait for it runs
+ * out.  The kernel then ORs BSA_DEVERR_TIMEOUT into the error word, every
+ * role of the CTA drains its loads and MMAs, frees its tensor memory and
+ * returns; the other CTAs finish normally.  No TMA load or MMA is ever counted
+ * on the withheld barrier.  No counterpart in the reference. */
+BSA_API int bsa_test_arm_wait_timeout(uint32_t wait_us);
 
 #ifdef __cplusplus
 }

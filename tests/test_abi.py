@@ -90,6 +90,8 @@ def test_other_entry_points_validate_on_host():
     assert L.bsa_build_tile_order(None, 1, 1, 4, 128, 0x1000, None) == 1               # no tile_ptr
     assert L.bsa_build_tile_order(0x1000, 1, 1, 4, 96, 0x2000, None) == 5              # block size
     assert L.bsa_blockmask_from_coords(None, None, 0, 0, 64, 1, 1, None, None, None, None, None) == 1
+    assert L.bsa_test_arm_wait_timeout(10) == 1                                       # below 100 us: refused
+    assert L.bsa_test_arm_wait_timeout(3_000_000) == 1                                # above 2 s: refused
     size = ctypes.c_size_t()
     assert L.bsa_fwd_reordered_workspace_bytes(ctypes.byref(_args()), ctypes.byref(size)) == 0
     # fused tcgen05 forward: k', v' of 1*2*256*64 bf16 each (Q and O go through the permutation in-kernel)
