@@ -87,6 +87,23 @@ class BlockSparsePlan:
     """
 
     def __init__(self, block_mask: torch.Tensor, block: int):
+        m = self._as_mask(block_mask)
+        self.mask_b, self.mask_h, self.nb = int(m.shape[0]), int(m.shape[1]), int(m.shape[2])
+        self.block = int(block)
+        self.device = m.device
+        L = _lib.lib()
+        ptr_len, cap, ws = ctypes.c_int64(), ctypes.c_int64(), ctypes.c_size_t()
+        _lib.check(L.bsa_plan_sizes(self.mask_b, self.mask_h, self.nb, self.block, ctypes.byref(ptr_len),
+                                    ctypes.byref(cap), ctypes.byref(ws)), "bsa_plan_sizes")
+        self.tile_ptr = torch.empty(ptr_len.value, dtype=torch.int32, device=self.device)
+        self.tile_col = torch.empty(max(1, cap.value), dtype=torch.int32, device=self.device)
+        self._ws_bytes = ws.value
+        self._work = torch.empty(max(1, (ws.value + 3) // 4), dtype=torch.int32, device=self.device)
+        self.tile_order = torch.empty(max(1, ptr_len.value - 1), dtype=torch.int32, device=self.device)
+        self._build(m)
+
+    @staticmethod
+    def _as_mask(block_mask: torch.Tensor) -> torch.Tensor:
         _require_cuda(block_mask, "block_mask")
         m = block_mask
         if m.dim() == 2:
@@ -99,23 +116,28 @@ class BlockSparsePlan:
             m = (m != 0).view(torch.uint8)
         if m.stride(3) != 1:
             m = m.contiguous()
-        self.mask_b, self.mask_h, self.nb = int(m.shape[0]), int(m.shape[1]), int(m.shape[2])
-        self.block = int(block)
-        self.device = m.device
-        L = _lib.lib()
-        ptr_len, cap, ws = ctypes.c_int64(), ctypes.c_int64(), ctypes.c_size_t()
-        _lib.check(L.bsa_plan_sizes(self.mask_b, self.mask_h, self.nb, self.block, ctypes.byref(ptr_len),
-                                    ctypes.byref(cap), ctypes.byref(ws)), "bsa_plan_sizes")
-        self.tile_ptr = torch.empty(ptr_len.value, dtype=torch.int32, device=self.device)
-        self.tile_col = torch.empty(max(1, cap.value), dtype=torch.int32, device=self.device)
-        work = torch.empty(max(1, (ws.value + 3) // 4), dtype=torch.int32, device=self.device)
-        self.tile_order = torch.empty(max(1, ptr_len.value - 1), dtype=torch.int32, device=self.device)
-        _lib.check(L.bsa_build_plan(m.data_ptr(), m.stride(0), m.stride(1), m.stride(2), self.mask_b, self.mask_h,
-                                    self.nb, self.block, self.tile_ptr.data_ptr(), self.tile_col.data_ptr(),
-                                    self.tile_order.data_ptr(), work.data_ptr(), ws.value, _stream(self.device)),
+        return m
+
+    def _build(self, m: torch.Tensor) -> None:
+        _lib.check(_lib.lib().bsa_build_plan(m.data_ptr(), m.stride(0), m.stride(1), m.stride(2), self.mask_b,
+                                             self.mask_h, self.nb, self.block, self.tile_ptr.data_ptr(),
+                                             self.tile_col.data_ptr(), self.tile_order.data_ptr(),
+                                             self._work.data_ptr(), self._ws_bytes, _stream(self.device)),
                    "bsa_build_plan")
         self._mask_ref = m  # keep the mask alive until the kernels ran
-        self._work = work
+
+    def update(self, block_mask: torch.Tensor) -> "BlockSparsePlan":
+        """Rebuild the plan from a new mask of the same shape into the same
+        device buffers (no allocation; enqueued on the current stream, so a
+        forward already enqueued with this plan still reads the old one)."""
+        m = self._as_mask(block_mask)
+        if (int(m.shape[0]), int(m.shape[1]), int(m.shape[2])) != (self.mask_b, self.mask_h, self.nb):
+            raise ValueError(f"mask shape {tuple(m.shape)} differs from the plan's "
+                             f"({self.mask_b}, {self.mask_h}, {self.nb}, {self.nb})")
+        if m.device != self.device:
+            raise ValueError("mask is on another device")
+        self._build(m)
+        return self
 
     @property
     def tiles_per_row(self) -> int:

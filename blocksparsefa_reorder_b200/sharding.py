@@ -63,10 +63,22 @@ def local_heads(H: int, rank: int, world_size: int) -> tuple:
     return partition_units(H, world_size)[rank]
 
 
-def gather_units(local: torch.Tensor, ranges: Sequence[tuple], dst: int = 0, group=None) -> Optional[torch.Tensor]:
-    """Collect per-rank shards ``[hi - lo, ...]`` (rank r holds units
-    ``ranges[r]``) into one ``[total, ...]`` tensor on rank ``dst``; other
-    ranks return ``None``.  Every rank takes the same send/recv steps."""
+def _global_rank(group, r: int) -> int:
+    """Global rank of rank ``r`` of ``group`` (point-to-point calls take global ranks)."""
+    return r if group is None else dist.get_global_rank(group, r)
+
+
+def gather_units(local: torch.Tensor, ranges: Sequence[tuple], dst: int = 0, group=None, async_op: bool = False,
+                 out: Optional[torch.Tensor] = None, offsets: Optional[Sequence[int]] = None):
+    """Collect per-rank shards ``[hi - lo, ...]`` (rank r of ``group`` holds
+    units ``ranges[r]``) into one ``[total, ...]`` tensor on group rank
+    ``dst``; other ranks get ``None``.  The receives are posted together
+    (``batch_isend_irecv``), so the shards arrive concurrently.  ``out`` /
+    ``offsets`` (on ``dst``): receive rank r's shard into
+    ``out[offsets[r]:offsets[r] + size]`` instead of a new tensor laid out by
+    ``ranges``.  With ``async_op`` the call returns ``(full_or_None, works)``
+    without waiting; wait on every work before reading the result (or reusing
+    ``local``)."""
     rank = dist.get_rank(group)
     world = dist.get_world_size(group)
     if len(ranges) != world:
@@ -74,15 +86,28 @@ def gather_units(local: torch.Tensor, ranges: Sequence[tuple], dst: int = 0, gro
     lo, hi = ranges[rank]
     if local.shape[0] != hi - lo:
         raise ValueError(f"rank {rank}: local shard has {local.shape[0]} units, expected {hi - lo}")
-    total = ranges[-1][1]
+    if offsets is None:
+        offsets = [r[0] for r in ranges]
+    elif len(offsets) != world:
+        raise ValueError("one offset per rank")
+    full, ops = None, []
     if rank == dst:
-        full = torch.empty((total,) + tuple(local.shape[1:]), dtype=local.dtype, device=local.device)
-        full[lo:hi].copy_(local)
+        if out is None:
+            total = max(o + (b - a) for o, (a, b) in zip(offsets, ranges))
+            out = torch.empty((total,) + tuple(local.shape[1:]), dtype=local.dtype, device=local.device)
+        full = out
+        if hi > lo:
+            full[offsets[rank]:offsets[rank] + hi - lo].copy_(local)
         for r in range(world):
             rlo, rhi = ranges[r]
             if r != dst and rhi > rlo:
-                dist.recv(full[rlo:rhi], src=r, group=group)
-        return full
-    if hi > lo:
-        dist.send(local.contiguous(), dst=dst, group=group)
-    return None
+                ops.append(dist.P2POp(dist.irecv, full[offsets[r]:offsets[r] + rhi - rlo], _global_rank(group, r),
+                                      group))
+    elif hi > lo:
+        ops.append(dist.P2POp(dist.isend, local.contiguous(), _global_rank(group, dst), group))
+    works = dist.batch_isend_irecv(ops) if ops else []
+    if async_op:
+        return full, works
+    for w in works:
+        w.wait()
+    return full

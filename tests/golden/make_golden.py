@@ -2,7 +2,7 @@
 
 Run on a machine that has the reference checkout (read-only is enough):
 
-    python tests/golden/make_golden.py --reference /root/reference
+    python tests/golden/make_golden.py --reference <path of the reference checkout>
 
 It imports the reference's own code from that checkout and records its
 outputs on small seeded inputs:
@@ -192,7 +192,7 @@ def make_attention(naive, fused, out: dict):
 
 def main():
     ap = argparse.ArgumentParser()
-    ap.add_argument("--reference", type=Path, default=Path("/root/reference"))
+    ap.add_argument("--reference", type=Path, required=True, help="path of the reference checkout")
     args = ap.parse_args()
     import numpy as np
 

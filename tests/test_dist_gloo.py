@@ -65,6 +65,46 @@ def test_sharded_units_gather_to_rank0(tmp_path):
     assert err == 0.0
 
 
+def _worker_subgroup(rank, world, port, out_dir):
+    """World of 3; ranks 1 and 2 form a subgroup and gather to the
+    subgroup's rank 0 (global rank 1): group ranks must be mapped to global
+    ranks for the point-to-point calls.  The second gather places the shards
+    at given offsets of a caller's tensor."""
+    try:
+        _init(rank, world, port)
+        sub = dist.new_group([1, 2])
+        if rank in (1, 2):
+            ranges = [(0, 2), (2, 5)]
+            grank = dist.get_rank(sub)
+            lo, hi = ranges[grank]
+            local = torch.arange(lo * 3, hi * 3, dtype=torch.float32).reshape(hi - lo, 3)
+            full, works = sharding.gather_units(local, ranges, dst=0, group=sub, async_op=True)
+            for w in works:
+                w.wait()
+            out = torch.zeros(7, 3) if grank == 0 else None
+            placed = sharding.gather_units(local, ranges, dst=0, group=sub, out=out, offsets=[5, 0])
+            if grank == 0:
+                ref = torch.arange(15, dtype=torch.float32).reshape(5, 3)
+                ok = torch.equal(full, ref) and torch.equal(placed[5:7], ref[0:2]) and torch.equal(placed[0:3],
+                                                                                                   ref[2:5])
+                with open(os.path.join(out_dir, "sub.txt"), "w") as f:
+                    f.write("ok" if ok else "mismatch")
+            else:
+                assert full is None and placed is None
+        dist.barrier()
+        dist.destroy_process_group()
+    except Exception:
+        with open(os.path.join(out_dir, f"fail{rank}.txt"), "w") as f:
+            f.write(traceback.format_exc())
+        raise
+
+
+def test_gather_over_subgroup(tmp_path):
+    port = _free_port()
+    mp.start_processes(_worker_subgroup, args=(3, port, str(tmp_path)), nprocs=3, join=True, start_method="spawn")
+    assert (tmp_path / "sub.txt").read_text() == "ok"
+
+
 def _worker_fail(rank, world, port, out_dir):
     _init(rank, world, port, timeout_s=5)
     if rank == 1:

@@ -191,13 +191,18 @@ def test_golden_reference_kernels(dev, golden_dir):
         assert np.abs(m[fin] - ref_M[fin]).max() <= TOL_LSE, name
 
 
-@pytest.mark.parametrize("block", [128, 64])
-def test_masked_blocks_contribute_nothing(dev, block):
+@pytest.mark.parametrize("block,N,p", [(128, 1024, 0.2), (64, 1024, 0.2), (64, 3072, 0.85)])
+def test_masked_blocks_contribute_nothing(dev, block, N, p):
     """NaN/Inf-poison every K/V row in key blocks that no query block keeps,
-    and perturb them: O must stay finite and bitwise equal."""
-    B, H, N, D = 1, 2, 1024, 128
+    and perturb them: O must stay finite and bitwise equal.  Then perturb (by
+    finite amounts) every key block the first block row does not keep: that
+    block row's output must stay bitwise equal, also at BLOCK 64 where the
+    perturbed blocks include ones its sibling row in the 128-row tile keeps
+    (loaded for the tile, scored and given P = 0 for these rows).  The last
+    case is dense enough for the paired BLOCK 64 form."""
+    B, H, D = 1, 2, 128
     nb = N // block
-    mask = _rand_mask(nb, 0.2, seed=21)
+    mask = _rand_mask(nb, p, seed=21)
     mask[..., :, nb - 2:] = False
     unused = np.nonzero(~mask[0, 0].any(axis=0))[0]
     assert unused.size > 0
@@ -218,8 +223,7 @@ def test_masked_blocks_contribute_nothing(dev, block):
         k3[:, :, j * block:(j + 1) * block] += 3.0
         v3[:, :, j * block:(j + 1) * block] -= 5.0
     o3 = block_sparse_attention(q, k3, v3, mt)
-    if block == 128:
-        assert torch.equal(o1[:, :, :block], o3[:, :, :block])
+    assert torch.equal(o1[:, :, :block], o3[:, :, :block])
 
 
 def test_tcgen05_vs_simt_crosscheck(dev):
@@ -412,13 +416,13 @@ def test_long_context_sampled(dev):
 
 
 @pytest.mark.parametrize("D", [64, 128])
-def test_block64_steps_pair_entries(dev, D):
-    """At BLOCK 64 the kernel takes a tile's kept key blocks two at a time
-    (one 128-key step).  Covered here: tiles with an odd number of kept
-    blocks (the last step has one), blocks kept by only one of the tile's two
-    query block rows, a tile whose rows keep disjoint blocks, a partial last
-    key block (N % 64 != 0) in either half of a step, and key blocks no query
-    keeps filled with NaN."""
+def test_block64_single_form_edges(dev, D):
+    """BLOCK 64 with a sparse plan (tiles average fewer than 32 kept blocks),
+    so the kernel form that runs one kept block per step is the one selected:
+    tiles with an odd number of kept blocks, blocks kept by only one of the
+    tile's two query block rows, a tile whose rows keep disjoint blocks, a
+    partial last key block (N % 64 != 0), and key blocks no query keeps filled
+    with NaN.  (The paired form's edges are covered in test_gpu_configs.py.)"""
     B, H, block = 1, 3, 64
     N = 64 * 13 + 23
     nb = (N + block - 1) // block
@@ -438,6 +442,7 @@ def test_block64_steps_pair_entries(dev, D):
     k[:, 2, 11 * block:12 * block] = float("nan")
     v[:, 2, 11 * block:12 * block] = float("nan")
     plan = BlockSparsePlan(torch.from_numpy(mask).to(dev), block)
+    assert plan.nnz_entries() < 32 * plan.mask_b * plan.mask_h * plan.tiles_per_row  # the single form runs
     o, lse = block_sparse_attention(q, k, v, plan=plan, kernel="tcgen05", return_lse=True, check_errors=True)
     kc, vc = k.clone(), v.clone()
     kc[:, 2, 11 * block:12 * block] = 0
