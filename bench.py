@@ -1,18 +1,34 @@
 """Benchmark: effective TFLOPS on kept blocks and ms per forward on B200.
 
-    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference] [--workload NAME]
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+                    [--workload NAME] [--scaling strong|weak] [--no-per-config]
 
 One step is one block-sparse attention forward of the workload through the
-library: the per-tile plan is built from the bool block mask on the GPU and
-the tcgen05 attention kernel runs over it (plus the row gather / scatter
-kernels when the workload carries a token permutation).  Inputs are resident
-in HBM when timing starts; K steps are timed with CUDA events between a
-barrier + synchronize on both sides; the max over ranks is reported.
+library: the tcgen05 attention kernel over the per-tile plan of the block
+mask (plus the K / V row-permutation kernels when the workload carries a
+token permutation; the query permutation is applied inside the attention
+kernel).  As in the reference's timed loop (BlockSparseTriton_Naive.py:
+131-161 reuses one block mask for every iteration), the plan is built once per
+mask before timing; the plan build is timed on its own and a second number
+rebuilds it every step.  Each step is replayed from a CUDA graph of the call
+(the same kernels the eager call launches, without per-step host work).
+Inputs are resident in HBM when timing starts; when one rank's inputs would
+fit in L2 the steps rotate over several input copies so that every step reads
+from DRAM.  K steps are timed with CUDA events between a barrier + synchronize
+on both sides; the max over ranks is reported.
 
-Default workload ``headline``: B1 H16 N16384 D128 bf16 BLOCK128, block mask =
-diagonal + Bernoulli(0.10), identity permutation (the "N=16K, D=128, 10%
-density" operating point).  With N GPUs every rank runs its own copy of the
-workload (weak scaling: 16 heads per rank), with no collective on the path.
+Default workload ``headline``: B1 H16 N16384 D128 bf16 BLOCK128, block mask
+= diagonal + Bernoulli(0.10), identity permutation (the "N=16K, D=128, 10%
+density" operating point).  Under torchrun the (b, h) units of the workload
+are split over the ranks (strong scaling, no collective; ``--scaling weak``
+gives every rank its own copy instead, and the strong run also reports the
+weak number).  The long-context workload gathers O to rank 0 inside the step
+(NCCL point-to-point over NVLink), as that configuration specifies.
+
+At N = 1 the line also carries ``per_config``: every benchmark configuration
+measured on this GPU (kernel time, TFLOP/s, roofline fractions, measured
+density, a max-abs-error spot check against an fp64 masked softmax on sampled
+query blocks).
 
 ``--impl reference`` times the CPU restatement of the reference's block loop
 (the oracle port: one float32 numpy program per query block, one process per
@@ -23,8 +39,8 @@ from __future__ import annotations
 
 import argparse
 import json
+import math
 import os
-import re
 import statistics
 import sys
 import threading
@@ -38,6 +54,15 @@ METRIC = "effective TFLOPS on nonzero blocks & ms/fwd (N=16K, D=128, 10% density
 UNIT = "TFLOP/s"
 FALLBACK_PEAKS = {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0}
 DTYPE_NAMES = {"torch.bfloat16": "bf16", "torch.float16": "fp16", "torch.float32": "f32"}
+L2_BYTES = 126 * 2**20
+CONFIGS = ["plumbing", "random", "sbm", "headline", "longctx", "sweep_p01", "sweep_p05", "sweep_p20", "sweep_p50"]
+# DRAM bytes per attention launch from one ncu capture of the same kernel on the
+# same workload (dram__bytes_read.sum + dram__bytes_write.sum), with the
+# command that produced it; --ncu-csv takes the figure from a capture instead.
+NCU_TRAFFIC = {
+    "headline": (249916160.0, "ncu --set full --clock-control none -k regex:attn_tcp -s 3 -c 1 "
+                              "python bench.py --steps 10 --warmup 3 --no-cpu-baseline (headline workload)"),
+}
 
 
 def load_peaks():
@@ -50,14 +75,20 @@ def load_peaks():
     return dict(FALLBACK_PEAKS), "fallback"
 
 
-def profile_traffic(name: str):
-    """DRAM bytes per launch of the attention kernel from the committed ncu
-    summary (its ``dram_bytes_per_launch_full: <number>`` line)."""
-    p = ROOT / "profiles" / f"attn_tcp_{name}.md"
-    if not p.exists():
-        return None
-    m = re.search(r"dram_bytes_per_launch_full:\s*([0-9.eE+]+)", p.read_text())
-    return float(m.group(1)) if m else None
+def ncu_csv_traffic(path):
+    """dram__bytes_read.sum + dram__bytes_write.sum of the first attention
+    launch in an ``ncu --page raw --csv`` export."""
+    import csv
+
+    rows = list(csv.reader(open(path)))
+    hdr = rows[0]
+    ir, iw, ik = (hdr.index(c) for c in ("dram__bytes_read.sum", "dram__bytes_write.sum", "Kernel Name"))
+    units = rows[1]
+    scale = {"byte": 1.0, "Kbyte": 1e3, "Mbyte": 1e6, "Gbyte": 1e9}
+    for r in rows[2:]:
+        if "attn_tcp" in r[ik]:
+            return float(r[ir]) * scale.get(units[ir], 1.0) + float(r[iw]) * scale.get(units[iw], 1.0)
+    return None
 
 
 class ClockSampler:
@@ -67,7 +98,7 @@ class ClockSampler:
                0x20: "sw_thermal_slowdown", 0x40: "hw_thermal_slowdown", 0x80: "hw_power_brake_slowdown",
                0x100: "display_clock_setting"}
 
-    def __init__(self, device_index: int, period_s: float = 0.01):
+    def __init__(self, device_index: int, period_s: float = 0.005):
         self.idx, self.period = device_index, period_s
         self.samples = []
         self._stop = threading.Event()
@@ -107,7 +138,7 @@ class ClockSampler:
             self._t.join()
         return False
 
-    def summary(self, t0: float, t1: float):
+    def summary(self, t0: float, t1: float, what: str):
         if not self.ok:
             return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvml unavailable"], "samples": 0}
         win = [s for s in self.samples if t0 <= s[0] <= t1] or self.samples[-3:]
@@ -117,7 +148,7 @@ class ClockSampler:
                 if r & bit:
                     seen.add(name)
         return {"sm_mhz": statistics.median([s[1] for s in win]) if win else None, "sm_max_mhz": self.max_mhz,
-                "reasons": sorted(seen), "samples": len(win)}
+                "reasons": sorted(seen), "samples": len(win), "window": what}
 
 
 def dist_setup():
@@ -159,6 +190,181 @@ def describe(wl) -> str:
             f"block density {wl.density:.4f}, {perm}")
 
 
+def config_dict(wl, world: int, scaling: str) -> dict:
+    """The workload as both arms print it (the same dict for the same run)."""
+    from blocksparsefa_reorder_b200.sharding import partition_units
+
+    units = wl.B * wl.H
+    per_rank = max(b - a for a, b in partition_units(units, world)) if scaling == "strong" else units
+    return {"workload": describe(wl), "B": wl.B, "H": wl.H, "N": wl.N, "D": wl.D, "block": wl.block,
+            "dtype": DTYPE_NAMES[str(wl.dtype)], "density": round(wl.density, 5), "nnz_blocks": wl.nnz_blocks,
+            "flops_per_forward": wl.flops, "permutation": wl.q_perm is not None,
+            "parallelism": (f"(b,h) units split over {world} rank(s), at most {per_rank} per rank"
+                            if scaling == "strong" else f"each of {world} rank(s) runs the whole workload")
+                           + ("; O gathered to rank 0 by NCCL point-to-point inside the step"
+                              if wl.name == "longctx" and scaling == "strong" and world > 1 else "; no collective")}
+
+
+def scaling_of(world: int, requested: str) -> str:
+    return "strong" if world > 1 and requested == "strong" else "weak"
+
+
+# ----------------------------------------------------------------------------- inputs and work
+def unit_slice(t, lo, hi):
+    """Units [lo, hi) of a [B, H, ...] tensor as [1, hi - lo, ...] (the whole tensor when all)."""
+    B, H = t.shape[:2]
+    if lo == 0 and hi == B * H:
+        return t
+    return t.reshape((B * H,) + tuple(t.shape[2:]))[lo:hi].unsqueeze(0)
+
+
+def algorithmic_bytes(wl, units: int) -> float:
+    """Q read + O write once, each head's kept key blocks of K and V once
+    (shared through L2 by the tiles of the head), and the plan (tile_ptr,
+    tile_order, at most one entry per kept block)."""
+    import numpy as np
+
+    elt = 4 if DTYPE_NAMES[str(wl.dtype)] == "f32" else 2
+    cols = np.nonzero(wl.mask.any(axis=0))[0]
+    key_rows = int(sum(min(wl.block, wl.N - j * wl.block) for j in cols))
+    T = (wl.nb * wl.block + 127) // 128
+    plan = 4 * (2 * T + 1 + int(wl.mask.sum()))
+    return float(elt * units * (2 * wl.N * wl.D + 2 * key_rows * wl.D) + plan)
+
+
+class Runner:
+    """A workload's units [lo, hi) resident on this GPU, its plan built once,
+    and a CUDA graph of one forward per input copy."""
+
+    def __init__(self, wl, dev, lo, hi, seed=None, copies=None, graphs=True):
+        import torch
+
+        from blocksparsefa_reorder_b200 import BlockSparsePlan
+
+        self.wl, self.dev, self.lo, self.hi = wl, dev, lo, hi
+        self.units = hi - lo
+        q, k, v = (unit_slice(t, lo, hi).contiguous() for t in wl.make_qkv(dev, seed=seed))
+        self.mask = wl.mask_tensor(dev)
+        self.plan = BlockSparsePlan(self.mask, wl.block)
+        self.qp = torch.from_numpy(wl.q_perm).to(dev) if wl.q_perm is not None else None
+        self.kp = torch.from_numpy(wl.kv_perm).to(dev) if wl.kv_perm is not None else None
+        per_copy = 4 * q.numel() * q.element_size()
+        if copies is None:
+            copies = min(32, max(1, math.ceil(2 * L2_BYTES / per_copy)))
+        self.sets = [(q, k, v, torch.empty_like(q))]
+        for _ in range(copies - 1):
+            self.sets.append((q.clone(), k.clone(), v.clone(), torch.empty_like(q)))
+        self.footprint = per_copy * copies
+        self.graphs = []
+        # warm the host-side caches and the kernels once per copy, then capture
+        for s in self.sets:
+            self.forward(s)
+        torch.cuda.synchronize(dev)
+        if graphs:
+            for s in self.sets:
+                g = torch.cuda.CUDAGraph()
+                with torch.cuda.graph(g):
+                    self.forward(s)
+                self.graphs.append(g)
+            torch.cuda.synchronize(dev)
+
+    def forward(self, s):
+        from blocksparsefa_reorder_b200 import block_sparse_attention
+
+        q, k, v, o = s
+        return block_sparse_attention(q, k, v, plan=self.plan, q_perm=self.qp, kv_perm=self.kp, out=o)
+
+    def step(self, i):
+        if self.graphs:
+            self.graphs[i % len(self.graphs)].replay()
+        else:
+            self.forward(self.sets[i % len(self.sets)])
+
+    @property
+    def flops(self):
+        return self.wl.flops * self.units / (self.wl.B * self.wl.H)
+
+    def launches_per_step(self):
+        n = 2 if self.wl.block == 64 else 1  # BLOCK 64: both kernel forms launch, the plan picks one
+        return n + (2 if self.kp is not None else 0)
+
+    def release(self):
+        self.graphs = []
+        self.sets = []
+
+
+def time_steps(run, steps, stream, world, per_step_events=False):
+    """Time ``steps`` steps between barrier + synchronize; returns (ms per
+    step max over ranks, per-step event durations on this rank)."""
+    import torch
+
+    evs = []
+    barrier(world)
+    torch.cuda.synchronize()
+    start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    start.record(stream)
+    for i in range(steps):
+        if per_step_events:
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record(stream)
+            run(i)
+            e1.record(stream)
+            evs.append((e0, e1))
+        else:
+            run(i)
+    end.record(stream)
+    torch.cuda.synchronize()
+    barrier(world)
+    ms = start.elapsed_time(end) / steps
+    return max_over_ranks(ms, world), [a.elapsed_time(b) for a, b in evs]
+
+
+def time_plan(plan, mask, stream, reps=20):
+    """Mean device time of one plan build (into the plan's own buffers)."""
+    import torch
+
+    for _ in range(3):
+        plan.update(mask)
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    for _ in range(reps):
+        plan.update(mask)
+    e1.record(stream)
+    torch.cuda.synchronize()
+    return e0.elapsed_time(e1) / reps
+
+
+def spot_check(wl, o, q, k, v, unit, qblocks):
+    """Max |o - fp64 masked softmax| over the rows of the given query blocks
+    (new token order) of one (b, h) unit, computed on the host."""
+    import numpy as np
+    import torch
+
+    def host(t):
+        return t.reshape((-1,) + tuple(t.shape[2:]))[unit].double().cpu()
+
+    qh, kh, vh, oh = (host(t) for t in (q, k, v, o))
+    if wl.kv_perm is not None:
+        kp = torch.from_numpy(wl.kv_perm)
+        kh, vh = kh[kp], vh[kp]
+    scale = 1.0 / math.sqrt(wl.D)
+    err = 0.0
+    for mb in qblocks:
+        r0, r1 = mb * wl.block, min(wl.N, (mb + 1) * wl.block)
+        rows = torch.arange(r0, r1) if wl.q_perm is None else torch.from_numpy(wl.q_perm[r0:r1])
+        cols = np.nonzero(wl.mask[mb])[0]
+        if cols.size == 0:
+            ref = torch.zeros(r1 - r0, wl.D, dtype=torch.float64)
+        else:
+            keys = torch.from_numpy(np.concatenate([np.arange(j * wl.block, min(wl.N, (j + 1) * wl.block))
+                                                    for j in cols]))
+            s = (qh[rows] @ kh[keys].T) * scale
+            ref = torch.softmax(s, dim=-1) @ vh[keys]
+        err = max(err, float((oh[rows] - ref).abs().max()))
+    return err
+
+
+# ----------------------------------------------------------------------------- CPU baselines
 def make_cpu_pool(wl):
     """The oracle port of the reference block loop over one head of the
     workload, one process per host core."""
@@ -183,136 +389,275 @@ def cpu_baseline(wl, target_s: float):
             passes += 1
         return {"value": flops / secs / 1e12, "unit": UNIT, "cores": pool.workers, "kind": "port",
                 "sample": f"{passes} pass(es) over all {wl.nb} query blocks of one (b,h) head of the workload "
-                          f"({secs:.2f} s); float32 numpy port of the reference block loop, one process per core",
-                "ms_fwd_extrapolated": 1e3 * secs / passes * wl.B * wl.H}
+                          f"({secs:.2f} s); float32 numpy port of the reference block loop, one process per core"}
 
 
+def cpu_dense_masked(wl, target_s: float):
+    """The dense-masked softmax attention in PyTorch on the host (float32,
+    every host thread): S = QK^T * scale over all keys, -inf outside the block
+    mask, softmax, PV, over query-row chunks of one head until ``target_s``;
+    reported as effective TFLOPS on the kept blocks it covered."""
+    import torch
+
+    from oracle.cpu_pool import host_cores
+
+    cores = host_cores()
+    torch.set_num_threads(cores)
+    g = torch.Generator().manual_seed(wl.seed)
+    q, k, v = (torch.randn(wl.N, wl.D, generator=g) for _ in range(3))
+    mask = torch.from_numpy(wl.mask)
+    scale = 1.0 / math.sqrt(wl.D)
+    bpc = max(1, 1024 // wl.block)
+    secs, flops, blocks_done, mb = 0.0, 0.0, 0, 0
+    while secs < target_s and mb < wl.nb:
+        m = mask[mb:mb + bpc]
+        r0, r1 = mb * wl.block, min(wl.N, (mb + m.shape[0]) * wl.block)
+        tm = m.repeat_interleave(wl.block, 0).repeat_interleave(wl.block, 1)[: r1 - r0, :wl.N]
+        t0 = time.perf_counter()
+        s = (q[r0:r1] @ k.T) * scale
+        s.masked_fill_(~tm, float("-inf"))
+        p = torch.nan_to_num(torch.softmax(s, dim=-1))
+        o = p @ v
+        secs += time.perf_counter() - t0
+        flops += 4.0 * wl.block * wl.block * wl.D * int(m.sum())
+        blocks_done += m.shape[0]
+        mb += bpc
+        del o
+    return {"value": flops / secs / 1e12, "unit": UNIT, "cores": cores, "kind": "port",
+            "sample": f"{blocks_done} of {wl.nb} query blocks of one (b,h) head ({secs:.2f} s); dense masked "
+                      f"softmax attention in float32 PyTorch on the host (all keys scored, -inf outside the mask)",
+            "ms_per_forward_extrapolated": 1e3 * secs * wl.nb / max(1, blocks_done) * wl.B * wl.H}
+
+
+# ----------------------------------------------------------------------------- reference arm
 def run_reference(args):
     if int(os.environ.get("RANK", "0")) != 0:
         return 0
     from blocksparsefa_reorder_b200 import workloads as W
 
     wl = W.make(args.workload)
+    world = int(os.environ.get("WORLD_SIZE", str(args.gpus)))
+    scaling = scaling_of(world, args.scaling)
     with make_cpu_pool(wl) as pool:
         all_qb = list(range(wl.nb))
         t_head = pool.run(all_qb)  # calibration pass
         per_step = args.ref_budget_s / (args.steps + args.warmup)
         n_qb = max(1, min(wl.nb, int(wl.nb * per_step / max(t_head, 1e-6))))
-        rates, cursor = [], 0
+        rates, times, cursor = [], [], 0
         for i in range(args.warmup + args.steps):
             qb = [(cursor + j) % wl.nb for j in range(n_qb)]
             cursor = (cursor + n_qb) % wl.nb
             dt = pool.run(qb)
             if i >= args.warmup:
                 rates.append(pool.flops(qb) / dt / 1e12)
+                times.append(dt)
         cores = pool.workers
     v = statistics.median(rates)
-    ms_fwd = wl.flops / (v * 1e12) * 1e3
     line = {
-        "impl": "reference", "metric": METRIC, "value": v, "unit": UNIT, "n_gpus": args.gpus, "steps": args.steps,
-        "warmup": args.warmup, "ms_per_step": ms_fwd, "higher_is_better": True, "scaling": "weak",
-        "vs_baseline": None, "dtype": "f32", "data": "synthetic (seeded mask, q/k/v ~ N(0,1))",
-        "config": {"workload": describe(wl)},
+        "impl": "reference", "metric": METRIC, "value": v, "unit": UNIT, "n_gpus": world, "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": 1e3 * statistics.mean(times), "higher_is_better": True,
+        "scaling": scaling, "vs_baseline": None, "dtype": "f32", "data": "synthetic (seeded mask, q/k/v ~ N(0,1))",
+        "config": config_dict(wl, world, scaling),
+        "step": f"{n_qb} query blocks of one (b,h) head of the workload (the measured sample)",
+        "ms_per_forward_extrapolated": wl.flops / (v * 1e12) * 1e3,
         "cpu_baseline": {"value": v, "unit": UNIT, "cores": cores, "kind": "port",
                          "sample": f"{n_qb} query blocks of one (b,h) head per step; float32 numpy port of the "
                                    "reference block loop (the reference has no CPU path of its own), one process "
                                    "per core"},
         "e2e": {"value": v, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
-        "note": "ms_per_step = the workload's kept-block flops at the measured rate",
     }
     print(json.dumps(line), flush=True)
     return 0
 
 
-def run_ours(args):
+# ----------------------------------------------------------------------------- per-config measurement
+def measure_config(name, dev, peaks, steps=10, warmup=3):
+    """One benchmark configuration on this GPU (the whole workload)."""
     import torch
 
-    from blocksparsefa_reorder_b200 import BlockSparsePlan, block_sparse_attention
+    from blocksparsefa_reorder_b200 import block_sparse_attention, permute_rows
+    from blocksparsefa_reorder_b200 import workloads as W
+
+    wl = W.make(name)
+    units = wl.B * wl.H
+    stream = torch.cuda.current_stream(dev)
+    run = Runner(wl, dev, 0, units)
+    for i in range(warmup):
+        run.step(i)
+    step_ms, evs = time_steps(run.step, steps, stream, 1, per_step_events=True)
+    kern_ms = statistics.mean(evs)
+    if run.kp is not None:
+        # the attention kernel alone: K and V already in the new order, the
+        # query permutation (fused into the kernel) still applied
+        q, k, v, o = run.sets[0]
+        k2 = permute_rows(k, run.kp, dim=2, inverse=False)
+        v2 = permute_rows(v, run.kp, dim=2, inverse=False)
+
+        def call():
+            block_sparse_attention(q, k2, v2, plan=run.plan, q_perm=run.qp, out=o)
+
+        call()
+        torch.cuda.synchronize()
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g):
+            call()
+        for _ in range(warmup):
+            g.replay()
+        _, evs = time_steps(lambda i: g.replay(), steps, stream, 1, per_step_events=True)
+        kern_ms = statistics.mean(evs)
+        del g, k2, v2
+    # correctness spot check of the whole step's output
+    run.step(0)
+    torch.cuda.synchronize()
+    q0, k0, v0, o0 = run.sets[0]
+    qbs = sorted({0, wl.nb // 2, wl.nb - 1})
+    err = max(spot_check(wl, o0, q0, k0, v0, u, qbs) for u in (0, units - 1))
+    t_plan = time_plan(run.plan, run.mask, stream)
+    tile_entries = run.plan.nnz_entries()
+    tiles = run.plan.mask_b * run.plan.mask_h * run.plan.tiles_per_row
+    flops = wl.flops
+    nbytes = algorithmic_bytes(wl, units)
+    tensor = wl.dtype != torch.float32
+    tf = flops / (kern_ms * 1e-3) / 1e12
+    gbs = nbytes / (kern_ms * 1e-3) / 1e9
+    peak_tf = float(peaks.get("bf16_tflops", FALLBACK_PEAKS["bf16_tflops"]))
+    peak_bw = float(peaks.get("hbm_gbs", FALLBACK_PEAKS["hbm_gbs"]))
+    t_tensor, t_hbm = flops / (peak_tf * 1e12), nbytes / (peak_bw * 1e9)
+    bound = ("tensor" if t_tensor >= t_hbm else "hbm") if tensor else "cuda-core fp32 (correctness path)"
+    out = {
+        "workload": describe(wl), "density": round(wl.density, 5), "nnz_blocks": wl.nnz_blocks,
+        "kernel": ("attn_simt_kernel" if not tensor else
+                   "attn_tcp_kernel " + ("paired" if wl.block == 64 and tile_entries >= 32 * tiles else
+                                         "single-block steps" if wl.block == 64 else "BLOCK128")),
+        "entries_per_tile": round(tile_entries / tiles, 2),
+        "kernel_ms": kern_ms, "step_ms": step_ms, "plan_build_ms": t_plan,
+        "tflops_kernel": tf, "tflops_step": flops / (step_ms * 1e-3) / 1e12,
+        "bound": bound,
+        "tensor_frac": tf / peak_tf if tensor else None,
+        "hbm_gbs": gbs, "hbm_frac": gbs / peak_bw,
+        "algorithmic_bytes": nbytes, "algorithmic_flops": flops,
+        "max_abs_err": err, "err_check": "fp64 masked softmax on the host, query blocks %s of (b,h) units 0 and %d"
+                                         % (qbs, units - 1),
+    }
+    run.release()
+    del run
+    torch.cuda.empty_cache()
+    return out
+
+
+# ----------------------------------------------------------------------------- our arm
+def run_ours(args):
+    import torch
+    import torch.distributed as dist
+
+    from blocksparsefa_reorder_b200 import block_sparse_attention, sharding
     from blocksparsefa_reorder_b200 import workloads as W
 
     rank, world, local = dist_setup()
     dev = torch.device("cuda", local)
     torch.cuda.set_device(dev)
-    wl = W.make(args.workload)
-    shard = args.shard_heads and world > 1
-    if shard:
-        # strong scaling: every rank draws the same full inputs and takes its range of heads
-        from blocksparsefa_reorder_b200 import sharding
-
-        ranges = sharding.partition_units(wl.H, world)
-        h0, h1 = ranges[rank]
-        q, k, v = (t[:, h0:h1] for t in wl.make_qkv(dev))
-    else:
-        q, k, v = wl.make_qkv(dev, seed=wl.seed + 1000 * rank)
-    mask = wl.mask_tensor(dev)
-    if shard and mask.dim() == 4 and mask.shape[1] > 1:
-        mask = mask[:, h0:h1]
-    qp = torch.from_numpy(wl.q_perm).to(dev) if wl.q_perm is not None else None
-    kp = torch.from_numpy(wl.kv_perm).to(dev) if wl.kv_perm is not None else None
-    o = torch.empty_like(q)
     stream = torch.cuda.current_stream(dev)
-    # plan build: one kernel for small masks (<= 4096 tiles, <= 1024 per slice, <= 96 KiB of mask), else
-    # count, scan, fill and work order; K and V permutation passes when kv_perm is given (the query
-    # permutation is applied inside the attention kernel); the attention kernel
-    ms = mask.shape
-    slices, nb = (ms[0] * ms[1], ms[-1]) if mask.dim() == 4 else (1, ms[-1])
-    tiles_per_slice = (nb * wl.block + 127) // 128
-    small = slices * tiles_per_slice <= 4096 and tiles_per_slice <= 1024 and slices * nb * nb <= 96 * 1024
-    # (BLOCK 64 launches two forms of the attention kernel; the plan's density picks the one that runs)
-    launches_per_step = (1 if small else 4) + (2 if kp is not None else 0) + (2 if wl.block == 64 else 1)
-    k_events = []
+    wl = W.make(args.workload)
+    peaks, peak_kind = load_peaks()
+    units_total = wl.B * wl.H
+    scaling = scaling_of(world, args.scaling)
+    strong = scaling == "strong"
+    ranges = sharding.partition_units(units_total, world) if strong else [(0, units_total)] * world
+    lo, hi = ranges[rank]
+    gather = strong and wl.name == "longctx"
+    run = Runner(wl, dev, lo, hi, seed=None if strong or world == 1 else wl.seed + 1000 * rank,
+                 graphs=not gather)
+    per_rank_flops = run.flops
 
-    def step(record=False):
-        plan = BlockSparsePlan(mask, wl.block)
-        if record:
-            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-            e0.record(stream)
-        block_sparse_attention(q, k, v, plan=plan, q_perm=qp, kv_perm=kp, out=o)
-        if record:
-            e1.record(stream)
-            k_events.append((e0, e1))
-        if shard:  # the full output on rank 0 (NCCL point-to-point over NVLink)
-            sharding.gather_units(o[0], ranges, dst=0)
+    if gather:
+        # long context: each rank's heads in two halves; a half's O goes to
+        # rank 0 (placed at its global head index) while the next half computes
+        q, k, v, o = run.sets[0]
+        full = torch.empty((units_total, wl.N, wl.D), dtype=q.dtype, device=dev) if rank == 0 else None
 
-    for _ in range(args.warmup):
-        step()
+        def halves(r):
+            U = ranges[r][1] - ranges[r][0]
+            return [(0, U // 2), (U // 2, U)]
+
+        def step(i):
+            works = []
+            for part in range(2):
+                a, b = halves(rank)[part]
+                if b > a:
+                    block_sparse_attention(q[:, a:b], k[:, a:b], v[:, a:b], plan=run.plan, out=o[:, a:b])
+                sizes = [halves(r)[part] for r in range(world)]
+                offs = [ranges[r][0] + sizes[r][0] for r in range(world)]
+                _, w = sharding.gather_units(o[0, a:b], sizes, dst=0, async_op=True, out=full, offsets=offs)
+                works += w
+            for w in works:
+                w.wait()
+    else:
+        step = run.step
+
+    for i in range(args.warmup):
+        step(i)
     torch.cuda.synchronize()
+    # untimed identical steps (~load_seconds) so the clock samples cover a loaded GPU
+    t_one, _ = time_steps(step, 3, stream, world)
+    n_load = max(1, int(args.load_seconds * 1e3 / max(t_one, 1e-3)))
     with ClockSampler(local) as clk:
-        time.sleep(0.05)
-        barrier(world)
+        t_load0 = time.time()
+        for i in range(n_load):
+            step(i)
         torch.cuda.synchronize()
         t_wall0 = time.time()
-        start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-        start.record(stream)
-        for _ in range(args.steps):
-            step(record=True)
-        end.record(stream)
-        torch.cuda.synchronize()
+        ms_step, evs = time_steps(step, args.steps, stream, world, per_step_events=True)
         t_wall1 = time.time()
-        barrier(world)
-    ms_step = max_over_ranks(start.elapsed_time(end), world) / args.steps
-    kern_ms = max_over_ranks(statistics.mean(a.elapsed_time(b) for a, b in k_events), world)
-    value = wl.flops * (1 if shard else world) / (ms_step * 1e-3) / 1e12
-    clocks = clk.summary(t_wall0, t_wall1)
+    kern_ms = max_over_ranks(statistics.mean(evs), world)
+    value = wl.flops * (1 if strong else world) / (ms_step * 1e-3) / 1e12
+    clocks = clk.summary(t_load0, t_wall1, "timed region and the %.2f s of identical steps before it"
+                         % (t_wall0 - t_load0))
+    clocks_timed = clk.summary(t_wall0, t_wall1, "timed region")
 
-    # e2e: the public API from pinned host buffers, copies inside the timed region.  Every step copies
-    # its own inputs host -> device and its output back; steps are pipelined over three streams (step
-    # i+1's inputs cross PCIe while step i computes and step i-1's output drains), with two sets of
+    # plan rebuilt every step (into the same buffers), eager calls
+    def step_with_plan(i):
+        run.plan.update(run.mask)
+        run.forward(run.sets[i % len(run.sets)])
+
+    ms_plan_step = None
+    if not gather:
+        for i in range(3):
+            step_with_plan(i)
+        ms_plan_step, _ = time_steps(step_with_plan, args.steps, stream, world)
+    t_plan = time_plan(run.plan, run.mask, stream)
+
+    # the weak-scaling number beside the strong one
+    weak = None
+    if strong and not gather:
+        run_w = Runner(wl, dev, 0, units_total, seed=wl.seed + 1000 * rank)
+        for i in range(3):
+            run_w.step(i)
+        ms_w, _ = time_steps(run_w.step, args.steps, stream, world)
+        weak = {"value": wl.flops * world / (ms_w * 1e-3) / 1e12, "ms_per_step": ms_w,
+                "what": "every rank runs the whole workload on its own inputs (replicas), no collective"}
+        run_w.release()
+        del run_w
+
+    # e2e: the public API from pinned host buffers, copies inside the timed
+    # region.  Every step copies its own inputs host -> device and its output
+    # back; steps are pipelined over copy streams (step i+1's inputs cross PCIe
+    # while step i computes and step i-1's output drains), with two sets of
     # device buffers.
+    q, k, v, o = run.sets[0]
     e2e_steps = max(3, min(args.steps, 10))
     hq, hk, hv = (t.cpu().pin_memory() for t in (q, k, v))
     hmask = wl.mask_tensor("cpu").pin_memory()
     hos = [torch.empty(o.shape, dtype=o.dtype).pin_memory() for _ in range(2)]
-    hqp = torch.from_numpy(wl.q_perm).pin_memory() if qp is not None else None
-    hkp = torch.from_numpy(wl.kv_perm).pin_memory() if kp is not None else None
-    hins = [t for t in (hq, hk, hv, hmask, hqp, hkp)]
+    hqp = torch.from_numpy(wl.q_perm).pin_memory() if run.qp is not None else None
+    hkp = torch.from_numpy(wl.kv_perm).pin_memory() if run.kp is not None else None
+    hins = [hq, hk, hv, hmask, hqp, hkp]
     dins = [[torch.empty(t.shape, dtype=t.dtype, device=dev) if t is not None else None for t in hins]
             for _ in range(2)]
     douts = [torch.empty_like(o) for _ in range(2)]
     s_h2d, s_d2h = torch.cuda.Stream(dev), torch.cuda.Stream(dev)
     ev = lambda: torch.cuda.Event()  # noqa: E731
-    freed = [None, None]  # compute of the step that last used buffer set b is done
-    drained = [None, None]  # d2h of the step that last used output buffer b is done
+    freed = [None, None]
+    drained = [None, None]
 
     def e2e_run(nsteps):
         for i in range(nsteps):
@@ -350,52 +695,71 @@ def run_ours(args):
     e2.record(stream)
     torch.cuda.synchronize()
     e2e_ms = max_over_ranks(s2.elapsed_time(e2) / e2e_steps, world)
-    ho = hos[0]
-    h2d = sum(t.numel() * t.element_size() for t in (hq, hk, hv, hmask))
-    h2d += sum(t.numel() * t.element_size() for t in (hqp, hkp) if t is not None)
-    d2h = ho.numel() * ho.element_size()
+    h2d = sum(t.numel() * t.element_size() for t in hins if t is not None)
+    d2h = hos[0].numel() * hos[0].element_size()
     barrier(world)
+    footprint, n_copies = run.footprint, len(run.sets)
+    launches = run.launches_per_step()
+    run.release()
+    del run, q, k, v, o, dins, douts
+    torch.cuda.empty_cache()
     if world > 1:
-        import torch.distributed as dist
-
         dist.destroy_process_group()
     if rank != 0:
         return 0
 
-    peaks, peak_kind = load_peaks()
+    per_config = None
+    if world == 1 and not args.no_per_config:
+        per_config = {}
+        for name in CONFIGS:
+            try:
+                per_config[name] = measure_config(name, dev, peaks)
+            except Exception as e:  # report, do not hide
+                per_config[name] = {"error": f"{type(e).__name__}: {e}"}
+
     peak = float(peaks.get("bf16_tflops", FALLBACK_PEAKS["bf16_tflops"]))
-    local_flops = wl.flops * (h1 - h0) / wl.H if shard else wl.flops
-    achieved = local_flops / (kern_ms * 1e-3) / 1e12
+    achieved = per_rank_flops / (kern_ms * 1e-3) / 1e12
+    traffic, traffic_src = None, None
+    if args.ncu_csv:
+        traffic, traffic_src = ncu_csv_traffic(args.ncu_csv), f"ncu capture {args.ncu_csv}"
+    elif wl.name in NCU_TRAFFIC and world == 1:
+        traffic, traffic_src = NCU_TRAFFIC[wl.name][0], "committed ncu capture: " + NCU_TRAFFIC[wl.name][1]
     line = {
         "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": args.steps,
-        "warmup": args.warmup, "ms_per_step": ms_step, "higher_is_better": True,
-        "scaling": "strong" if shard else "weak",
+        "warmup": args.warmup, "ms_per_step": ms_step, "higher_is_better": True, "scaling": scaling,
         "vs_baseline": None, "dtype": DTYPE_NAMES[str(wl.dtype)],
         "data": "synthetic: seeded block mask; q, k, v ~ N(0,1) drawn on the device",
-        "config": {"workload": describe(wl), "B": wl.B, "H_per_rank": (h1 - h0) if shard else wl.H, "N": wl.N,
-                   "D": wl.D,
-                   "block": wl.block, "nnz_blocks_per_rank": wl.nnz_blocks, "density": round(wl.density, 5),
-                   "flops_per_rank": wl.flops / world if shard else wl.flops,
-                   "parallelism": (f"heads sharded over {world} ranks, O gathered to rank 0 by NCCL point-to-point "
-                                   f"inside the step" if shard else f"(b,h) units, {world} rank(s), no collective"),
-                   "l2": "inputs larger than L2 (q, k, v, o = %d MiB per rank); no flush" %
-                         (4 * q.numel() * q.element_size() // 2**20)},
+        "config": config_dict(wl, world, scaling),
+        "setup": {
+            "units_per_rank": [b - a for a, b in ranges],
+            "step": "attention forward with the plan built once per mask (the reference's timed loop reuses "
+                    "its block mask), replayed from a CUDA graph of the call" if not gather else
+                    "attention forward per half of the rank's heads with the O gather to rank 0 posted after "
+                    "each half (eager calls)",
+            "l2": ("inputs larger than L2: %d input cop%s of q, k, v, o, %d MiB per rank, rotated per step"
+                   % (n_copies, "y" if n_copies == 1 else "ies", footprint // 2**20))},
         "roofline": {"bound": "tensor", "achieved": achieved, "peak": peak, "unit": "TFLOP/s",
-                     "frac": achieved / peak, "traffic": profile_traffic(wl.name),
+                     "frac": achieved / peak, "traffic": traffic, "traffic_source": traffic_src,
                      "kernel": "attn_tcp_kernel", "kernel_ms": kern_ms,
+                     "algorithmic_flops_per_launch": per_rank_flops,
                      "peak_source": f"bf16_tflops (burst) of {peak_kind} peaks"},
-        "e2e": {"value": wl.flops * (1 if shard else world) / (e2e_ms * 1e-3) / 1e12, "unit": UNIT,
-                "ms_per_step": e2e_ms,
-                "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
-                "path": "block_sparse_attention(q, k, v, mask) from pinned host buffers; per step H2D of "
-                        "q, k, v, mask (+perms) and D2H of o, pipelined across steps on copy streams"},
-        "gpu_launches": launches_per_step * args.steps,
-        "clocks": clocks,
+        "plan_build_ms": t_plan,
+        "with_plan_build": None if ms_plan_step is None else {
+            "value": wl.flops * (1 if strong else world) / (ms_plan_step * 1e-3) / 1e12,
+            "ms_per_step": ms_plan_step, "what": "plan rebuilt from the mask every step (eager calls)"},
+        "weak": weak,
+        "e2e": {"value": wl.flops * (1 if strong else world) / (e2e_ms * 1e-3) / 1e12, "unit": UNIT,
+                "ms_per_step": e2e_ms, "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
+                "path": "block_sparse_attention(q, k, v, mask) from pinned host buffers (plan built inside each "
+                        "call); per step H2D of q, k, v, mask (+perms) and D2H of o, pipelined on copy streams"},
+        "gpu_launches": launches * args.steps,
+        "clocks": clocks, "clocks_timed_region": clocks_timed,
     }
-    if not args.no_cpu_baseline:
-        cb = cpu_baseline(wl, args.cpu_seconds)
-        cb.pop("ms_fwd_extrapolated", None)
-        line["cpu_baseline"] = cb
+    if per_config is not None:
+        line["per_config"] = per_config
+    if not args.no_cpu_baseline and world == 1:
+        line["cpu_baseline"] = cpu_baseline(wl, args.cpu_seconds)
+        line["cpu_dense_masked"] = cpu_dense_masked(wl, args.cpu_seconds)
     print(json.dumps(line), flush=True)
     return 0
 
@@ -403,16 +767,19 @@ def run_ours(args):
 def main(argv=None):
     ap = argparse.ArgumentParser(description=__doc__, formatter_class=argparse.RawDescriptionHelpFormatter)
     ap.add_argument("--gpus", type=int, default=1)
-    ap.add_argument("--steps", type=int, default=200)
+    ap.add_argument("--steps", type=int, default=100)
     ap.add_argument("--warmup", type=int, default=10)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--workload", default="headline")
+    ap.add_argument("--scaling", choices=["strong", "weak"], default="strong",
+                    help="under torchrun: split the workload's (b,h) units over the ranks (strong) or give every "
+                         "rank a copy (weak)")
+    ap.add_argument("--load-seconds", type=float, default=1.0, help="untimed identical steps before timing")
     ap.add_argument("--cpu-seconds", type=float, default=10.0, help="CPU baseline sample length")
     ap.add_argument("--ref-budget-s", type=float, default=90.0, help="total CPU time of the reference arm")
     ap.add_argument("--no-cpu-baseline", action="store_true")
-    ap.add_argument("--shard-heads", action="store_true",
-                    help="under torchrun: split the workload's heads over the ranks (strong scaling) and gather "
-                         "O to rank 0 inside each step, as the long-context configuration specifies")
+    ap.add_argument("--no-per-config", action="store_true")
+    ap.add_argument("--ncu-csv", default=None, help="ncu raw CSV of the same command: roofline traffic from it")
     args = ap.parse_args(argv)
     if args.warmup < 3:
         ap.error("--warmup must be >= 3")
