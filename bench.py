@@ -236,12 +236,13 @@ class Runner:
     """A workload's units [lo, hi) resident on this GPU, its plan built once,
     and a CUDA graph of one forward per input copy."""
 
-    def __init__(self, wl, dev, lo, hi, seed=None, copies=None, graphs=True):
+    def __init__(self, wl, dev, lo, hi, seed=None, copies=None, graphs=True, kernel="auto"):
         import torch
 
         from blocksparsefa_reorder_b200 import BlockSparsePlan
 
         self.wl, self.dev, self.lo, self.hi = wl, dev, lo, hi
+        self.kernel = kernel if str(wl.dtype) != "torch.float32" else "auto"
         self.units = hi - lo
         q, k, v = (unit_slice(t, lo, hi).contiguous() for t in wl.make_qkv(dev, seed=seed))
         self.mask = wl.mask_tensor(dev)
@@ -272,7 +273,8 @@ class Runner:
         from blocksparsefa_reorder_b200 import block_sparse_attention
 
         q, k, v, o = s
-        return block_sparse_attention(q, k, v, plan=self.plan, q_perm=self.qp, kv_perm=self.kp, out=o)
+        return block_sparse_attention(q, k, v, plan=self.plan, q_perm=self.qp, kv_perm=self.kp, out=o,
+                                      kernel=self.kernel)
 
     def step(self, i):
         if self.graphs:
@@ -471,7 +473,7 @@ def run_reference(args):
 
 
 # ----------------------------------------------------------------------------- per-config measurement
-def measure_config(name, dev, peaks, steps=10, warmup=3):
+def measure_config(name, dev, peaks, steps=10, warmup=3, kernel="auto"):
     """One benchmark configuration on this GPU (the whole workload)."""
     import torch
 
@@ -481,7 +483,7 @@ def measure_config(name, dev, peaks, steps=10, warmup=3):
     wl = W.make(name)
     units = wl.B * wl.H
     stream = torch.cuda.current_stream(dev)
-    run = Runner(wl, dev, 0, units)
+    run = Runner(wl, dev, 0, units, kernel=kernel)
     for i in range(warmup):
         run.step(i)
     step_ms, evs = time_steps(run.step, steps, stream, 1, per_step_events=True)
@@ -494,7 +496,7 @@ def measure_config(name, dev, peaks, steps=10, warmup=3):
         v2 = permute_rows(v, run.kp, dim=2, inverse=False)
 
         def call():
-            block_sparse_attention(q, k2, v2, plan=run.plan, q_perm=run.qp, out=o)
+            block_sparse_attention(q, k2, v2, plan=run.plan, q_perm=run.qp, out=o, kernel=run.kernel)
 
         call()
         torch.cuda.synchronize()
@@ -566,7 +568,7 @@ def run_ours(args):
     lo, hi = ranges[rank]
     gather = strong and wl.name == "longctx"
     run = Runner(wl, dev, lo, hi, seed=None if strong or world == 1 else wl.seed + 1000 * rank,
-                 graphs=not gather)
+                 graphs=not gather, kernel=args.kernel)
     per_rank_flops = run.flops
 
     if gather:
@@ -584,7 +586,8 @@ def run_ours(args):
             for part in range(2):
                 a, b = halves(rank)[part]
                 if b > a:
-                    block_sparse_attention(q[:, a:b], k[:, a:b], v[:, a:b], plan=run.plan, out=o[:, a:b])
+                    block_sparse_attention(q[:, a:b], k[:, a:b], v[:, a:b], plan=run.plan, out=o[:, a:b],
+                                           kernel=run.kernel)
                 sizes = [halves(r)[part] for r in range(world)]
                 offs = [ranges[r][0] + sizes[r][0] for r in range(world)]
                 _, w = sharding.gather_units(o[0, a:b], sizes, dst=0, async_op=True, out=full, offsets=offs)
@@ -646,7 +649,7 @@ def run_ours(args):
     # the weak-scaling number beside the strong one
     weak = None
     if strong and not gather:
-        run_w = Runner(wl, dev, 0, units_total, seed=wl.seed + 1000 * rank)
+        run_w = Runner(wl, dev, 0, units_total, seed=wl.seed + 1000 * rank, kernel=args.kernel)
         for i in range(3):
             run_w.step(i)
         ms_w, _ = time_steps(run_w.step, args.steps, stream, world)
@@ -728,9 +731,9 @@ def run_ours(args):
     per_config = None
     if world == 1 and not args.no_per_config:
         per_config = {}
-        for name in CONFIGS:
+        for name in args.configs.split(","):
             try:
-                per_config[name] = measure_config(name, dev, peaks)
+                per_config[name] = measure_config(name, dev, peaks, kernel=args.kernel)
             except Exception as e:  # report, do not hide
                 per_config[name] = {"error": f"{type(e).__name__}: {e}"}
 
@@ -798,6 +801,8 @@ def main(argv=None):
     ap.add_argument("--ref-budget-s", type=float, default=90.0, help="total CPU time of the reference arm")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-per-config", action="store_true")
+    ap.add_argument("--kernel", default="auto", help="kernel choice passed to block_sparse_attention")
+    ap.add_argument("--configs", default=",".join(CONFIGS), help="configurations of the per-config object")
     ap.add_argument("--ncu-csv", default=None, help="ncu raw CSV of the same command: roofline traffic from it")
     args = ap.parse_args(argv)
     if args.warmup < 3:
