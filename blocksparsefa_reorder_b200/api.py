@@ -186,11 +186,9 @@ def block_sparse_attention(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor,
     index at new position ``i``), or the runners' expanded ``[B,H,N,D]``
     views.  Inputs are taken in the ORIGINAL order and the output is returned
     in the ORIGINAL order (``BlockSparseTriton_Naive.py:129-161``).  On the
-    tensor-core path both permutations are applied inside the attention
-    kernel (Q rows gathered, K / V rows gathered by TMA, O / lse rows
-    scattered), as in ``BlockSparse_Fused.py:115-223``; K / V layouts without
-    a row view are permuted into a workspace first; the fp32 path permutes
-    every tensor.
+    tensor-core path the query permutation is applied inside the attention
+    kernel (Q rows gathered, O / lse rows scattered) and K, V are permuted by
+    one pass each into a workspace; the fp32 path permutes every tensor.
     return_lse: also return the per-row log-sum-exp in log2 units (the
     reference kernel's ``M``), ``-inf`` for rows that keep no block.
     check_errors: synchronise and raise if a device-side check fired.

@@ -52,17 +52,9 @@ size_t round256(size_t x) { return (x + 255) & ~size_t(255); }
 int launch_tc(const bsa_fwd_args* a, cudaStream_t st) { return launch_attn_tcp(a, st); }
 
 // The fused reordered forward: the tcgen05 kernel gathers Q rows and
-// scatters O / lse rows through q_perm itself, and gathers K / V rows through
-// kv_perm when both tensors have a row view (every [B,H,N,D] layout whose b
-// and h strides are multiples of its row stride); otherwise K and V are
-// permuted into the workspace beforehand.
+// scatters O / lse rows through q_perm itself; only K and V are permuted
+// beforehand.
 bool fused_reorder(const bsa_fwd_args* a) { return a->kernel != BSA_KERNEL_SIMT && attn_tc_supported(a); }
-
-bool fused_kv_gather(const bsa_fwd_args* a) {
-  int64_t rb, rh, rows;
-  return fused_reorder(a) && rows_gatherable(a->k, a->B, a->H, a->N, &rb, &rh, &rows) &&
-         rows_gatherable(a->v, a->B, a->H, a->N, &rb, &rh, &rows);
-}
 
 // Workspace layout of bsa_fwd_reordered, 256-byte aligned regions:
 //   [q'] [k' v'] [o' lse'] [check] -- k', v' when kv_perm is given; q', o',
@@ -170,7 +162,7 @@ extern "C" int bsa_fwd_reordered_workspace_bytes(const bsa_fwd_args* a, size_t* 
   if (!a || !bytes) return BSA_ERR_INVALID_ARG;
   const int rc = validate_fwd(a);
   if (rc) return rc;
-  *bytes = reorder_layout(a, !fused_reorder(a), !fused_kv_gather(a), a->err_flag != nullptr).total;
+  *bytes = reorder_layout(a, !fused_reorder(a), true, a->err_flag != nullptr).total;
   return BSA_OK;
 }
 
@@ -180,9 +172,8 @@ extern "C" int bsa_fwd_reordered(const bsa_fwd_args* a, const void* q_perm, cons
   if (rc) return rc;
   if ((q_perm || kv_perm) && perm_dtype != BSA_INDEX_I32 && perm_dtype != BSA_INDEX_I64) return BSA_ERR_DTYPE;
   const bool fused = fused_reorder(a);
-  const bool kv_gather = kv_perm && fused_kv_gather(a);
   const bool check = a->err_flag && (q_perm || kv_perm);
-  const ReorderLayout L = reorder_layout(a, !fused && q_perm != nullptr, kv_perm != nullptr && !kv_gather, check);
+  const ReorderLayout L = reorder_layout(a, !fused && q_perm != nullptr, kv_perm != nullptr, check);
   if (L.total && (!workspace || workspace_bytes < L.total)) return BSA_ERR_WORKSPACE;
   if ((rc = check_device())) return rc;
   cudaStream_t st = static_cast<cudaStream_t>(stream);
@@ -200,7 +191,6 @@ extern "C" int bsa_fwd_reordered(const bsa_fwd_args* a, const void* q_perm, cons
       return rc;
   }
   if (fused) {
-    if (kv_gather) return launch_attn_tcp(&inner, st, q_perm, perm_dtype, kv_perm);
     if (kv_perm) {
       inner.k = contiguous(ws + L.k, a);
       inner.v = contiguous(ws + L.v, a);

@@ -93,13 +93,7 @@ struct TcpParams {
   const uint8_t* q;           // query base, for the gather of permuted rows
   int64_t qs_b, qs_h, qs_n;   // query strides in elements
   const void* q_perm;         // optional query permutation (new row -> old row)
-  const void* kv_perm;        // optional key permutation: K / V rows gathered through it
-  int perm_dtype;             // bsa_index_dtype of q_perm and kv_perm
-  // with kv_perm, tmK / tmV are 2-D maps over rows of D elements; row of
-  // (b, h, n) = b * k_rb + h * k_rh + n (resp. v_*), rows >= k_rows / v_rows
-  // are outside the map (zero fill)
-  int64_t k_rb, k_rh, v_rb, v_rh;
-  int k_rows, v_rows;
+  int perm_dtype;             // bsa_index_dtype of q_perm
   int H, N, nb, T, mask_b, mask_h, total_tiles;
   int slot;  // work counter slot
   float scale_log2;
@@ -286,111 +280,61 @@ __global__ void __launch_bounds__(kThreadsP, 1)
 
   if (warp < 4) {
     regs_dec<kRegsIssueP>();
-    if (warp == 0) {
+    if (warp == 0 && lane == 0) {
       // ------------------------------------------------------------ producer
-      // Lane 0 claims tiles, waits for stages and arms the barriers; without a
-      // key permutation it also issues every load.  With one (the fused
-      // variant of BlockSparse_Fused.py:54-99), every lane gathers K / V rows
-      // through kv_perm, four rows per TMA gather.
-      const bool gather = p.kv_perm != nullptr;
-      if (lane == 0) {
-        tma_prefetch_desc(&tmQ);
-        tma_prefetch_desc(&tmK);
-        tma_prefetch_desc(&tmV);
-      }
+      tma_prefetch_desc(&tmQ);
+      tma_prefetch_desc(&tmK);
+      tma_prefetch_desc(&tmV);
       int e = 0, g = 0, gv = 0;  // non-empty tiles, K steps, V steps loaded so far
       int pv_b = 0, pv_h = 0;    // the step whose V is still to load (gv < g)
       int pv_kb[C::SUB] = {};
       bool ok = true;
       int armed = 0;   // kv_full phases armed so far (one per step, one more for the last V)
       int qarmed = 0;  // Q tiles loaded by TMA so far
-      // lane 0 waits, every lane gets the outcome
-      auto wait0 = [&](uint64_t* bar, uint32_t parity) -> bool {
-        int r = 1;
-        if (lane == 0) r = mbar_wait(bar, parity, abort_flag, p.err, p.wait_ns) ? 1 : 0;
-        return __shfl_sync(0xffffffffu, r, 0) != 0;
-      };
       // the barrier of step gs's K may be re-armed once S_gs-KS completed: the commit
       // after PV_gs-KS-1 (S_0 and S_1 both under the one after PV_0)
       auto wait_k_stage = [&](int gs) -> bool {
         const int sd = gs - KS - 1 > 0 ? gs - KS - 1 : 0;
-        return gs < KS || wait0(&step_done[sd & 3], (sd >> 2) & 1);
+        return gs < KS || mbar_wait(&step_done[sd & 3], (sd >> 2) & 1, abort_flag, p.err, p.wait_ns);
       };
       // V_gv's stage is free once PV_gv-VS completed
       auto wait_v_stage = [&]() -> bool {
-        return gv < VS || wait0(&step_done[(gv - VS) & 3], ((gv - VS) >> 2) & 1);
-      };
-      // key block kb of (b, h) into one entry's rows of a stage: one box load
-      // per 64-column chunk (lane 0), or gathers of four permuted rows (lane l
-      // takes rows 4l .. 4l+3; keys at or past N read zeros and are masked)
-      auto load_block = [&](uint8_t* dst, const CUtensorMap* tm, uint64_t* bar, int kb, int h, int b, int64_t rb,
-                            int64_t rh, int rows) {
-        if (!gather) {
-          if (lane == 0)
-            for (int c = 0; c < C::NCHUNK; ++c) tma_load_4d(dst + c * C::KV_CHUNK, tm, bar, c * 64, kb * BN, h, b);
-        } else if (lane < BN / 4) {
-          int r[4];
-#pragma unroll
-          for (int u = 0; u < 4; ++u) {
-            const int n = kb * BN + lane * 4 + u;
-            r[u] = rows;
-            if (n < p.N) {
-              const int64_t old = load_perm(p.kv_perm, p.perm_dtype, n);
-              if (old >= 0 && old < p.N)
-                r[u] = static_cast<int>(b * rb + h * rh + old);
-              else
-                set_err(p.err, BSA_DEVERR_PERM_RANGE);
-            }
-          }
-          for (int c = 0; c < C::NCHUNK; ++c)
-            tma_gather4(dst + c * C::KV_CHUNK + lane * 512, tm, bar, c * 64, r[0], r[1], r[2], r[3]);
-        }
+        return gv < VS || mbar_wait(&step_done[(gv - VS) & 3], ((gv - VS) >> 2) & 1, abort_flag, p.err, p.wait_ns);
       };
       // V_gv into its stage, counted on the barrier of the step it travels with (bar)
       auto load_v = [&](uint64_t* bar) {
         const int st = gv % VS;
 #pragma unroll
         for (int u = 0; u < C::SUB; ++u)
-          load_block(sV + st * C::KV_BYTES + u * C::BOX_BYTES, &tmV, bar, pv_kb[u], pv_h, pv_b, p.v_rb, p.v_rh,
-                     p.v_rows);
+          for (int c = 0; c < C::NCHUNK; ++c)
+            tma_load_4d(sV + st * C::KV_BYTES + c * C::KV_CHUNK + u * C::BOX_BYTES, &tmV, bar, c * 64,
+                        pv_kb[u] * BN, pv_h, pv_b);
         ++gv;
       };
       for (int i = 0; ok; ++i) {
         // claim the next tile and pass its number on
-        int w = -1, e0 = 0, n = 0, b = 0, h = 0, t = 0;
-        if (lane == 0) {
-          const uint32_t claim = atomicAdd(&g_work_next[p.slot], 1u);
-          w = claim < static_cast<uint32_t>(p.total_tiles) ? static_cast<int>(claim) : -1;
-          if (w >= 0) tile_info(w, e0, n, b, h, t);
-        }
-        w = __shfl_sync(0xffffffffu, w, 0);
-        e0 = __shfl_sync(0xffffffffu, e0, 0);
-        n = __shfl_sync(0xffffffffu, n, 0);
-        b = __shfl_sync(0xffffffffu, b, 0);
-        h = __shfl_sync(0xffffffffu, h, 0);
-        t = __shfl_sync(0xffffffffu, t, 0);
+        const uint32_t claim = atomicAdd(&g_work_next[p.slot], 1u);
+        const int w = claim < static_cast<uint32_t>(p.total_tiles) ? static_cast<int>(claim) : -1;
         const int ri = i % kTileRing;
-        if (i >= kTileRing && !(ok = wait0(&tile_free[ri], ((i / kTileRing) - 1) & 1))) break;
-        if (lane == 0) {
-          tile_ring[ri].w = w;
-          tile_ring[ri].e0 = e0;
-          tile_ring[ri].n = n;
-          tile_ring[ri].b = b;
-          tile_ring[ri].h = h;
-          tile_ring[ri].t = t;
-          mbar_arrive(&tile_ready[ri]);  // release: the entry is visible to every waiter
-        }
+        int e0 = 0, n = 0, b = 0, h = 0, t = 0;
+        if (w >= 0) tile_info(w, e0, n, b, h, t);
+        if (i >= kTileRing && !(ok = mbar_wait(&tile_free[ri], ((i / kTileRing) - 1) & 1, abort_flag, p.err, p.wait_ns))) break;
+        tile_ring[ri].w = w;
+        tile_ring[ri].e0 = e0;
+        tile_ring[ri].n = n;
+        tile_ring[ri].b = b;
+        tile_ring[ri].h = h;
+        tile_ring[ri].t = t;
+        mbar_arrive(&tile_ready[ri]);  // release: the entry is visible to every waiter
         if (w < 0) break;
         if (n == 0) continue;
         const int qb = e & 1;
         if (!p.q_perm) {  // (permuted queries: warps 2-3 gather Q)
-          if (e >= 2 && !(ok = wait0(&q_empty[qb], ((e >> 1) - 1) & 1))) break;
-          if (lane == 0) {
-            mbar_arrive_expect_tx(&q_full[qb], C::Q_BYTES);
-            for (int c = 0; c < C::NCHUNK; ++c)
-              tma_load_4d(sQ + qb * C::Q_BYTES + c * C::Q_CHUNK, &tmQ, &q_full[qb], c * 64, t * 128, h, b);
-          }
+          if (e >= 2 && !(ok = mbar_wait(&q_empty[qb], ((e >> 1) - 1) & 1, abort_flag, p.err, p.wait_ns))) break;
+          mbar_arrive_expect_tx(&q_full[qb], C::Q_BYTES);
           ++qarmed;
+          for (int c = 0; c < C::NCHUNK; ++c)
+            tma_load_4d(sQ + qb * C::Q_BYTES + c * C::Q_CHUNK, &tmQ, &q_full[qb], c * 64, t * 128, h, b);
         }
         ++e;
         const int nsteps = (n + C::SUB - 1) / C::SUB;
@@ -402,30 +346,28 @@ __global__ void __launch_bounds__(kThreadsP, 1)
           for (int u = 0; u < C::SUB; ++u) {
             // a missing second entry (odd count) repeats the first: the softmax masks it out
             const int ei = j * C::SUB + u < n ? j * C::SUB + u : j * C::SUB;
-            kb[u] = static_cast<int>(static_cast<uint32_t>(__ldg(&p.tile_col[e0 + ei])) & 0xFFFFFFu);
+            kb[u] = static_cast<int>(static_cast<uint32_t>(p.tile_col[e0 + ei]) & 0xFFFFFFu);
             if (kb[u] >= p.nb) {
-              if (lane == 0) set_err(p.err, BSA_DEVERR_PLAN);
+              set_err(p.err, BSA_DEVERR_PLAN);
               kb[u] = 0;
             }
           }
           // K_g and (from the second step on) V_g-1 complete one phase of
-          // kv_full[st]: each load's bytes are announced before any is issued
+          // kv_full[st]: each load's bytes are announced before it is issued
           // and the phase's one arrival comes last, so a V stage that never
           // frees (a role gave up) leaves a phase that completes with K alone
           ++armed;
-          if (lane == 0) mbar_expect_tx(&kv_full[st], C::KV_BYTES);
-          __syncwarp();
+          mbar_expect_tx(&kv_full[st], C::KV_BYTES);
 #pragma unroll
           for (int u = 0; u < C::SUB; ++u)
-            load_block(sK + st * C::KV_BYTES + u * C::BOX_BYTES, &tmK, &kv_full[st], kb[u], h, b, p.k_rb, p.k_rh,
-                       p.k_rows);
+            for (int c = 0; c < C::NCHUNK; ++c)
+              tma_load_4d(sK + st * C::KV_BYTES + c * C::KV_CHUNK + u * C::BOX_BYTES, &tmK, &kv_full[st], c * 64,
+                          kb[u] * BN, h, b);
           if (gv < g && (ok = wait_v_stage())) {
-            if (lane == 0) mbar_expect_tx(&kv_full[st], C::KV_BYTES);
-            __syncwarp();
+            mbar_expect_tx(&kv_full[st], C::KV_BYTES);
             load_v(&kv_full[st]);
           }
-          __syncwarp();
-          if (lane == 0) mbar_arrive(&kv_full[st]);
+          mbar_arrive(&kv_full[st]);
           if (!ok) break;
           pv_b = b;
           pv_h = h;
@@ -437,23 +379,18 @@ __global__ void __launch_bounds__(kThreadsP, 1)
         // the last V alone, on the barrier of step g (no K)
         if ((ok = wait_k_stage(g) && wait_v_stage())) {
           ++armed;
-          if (lane == 0) mbar_expect_tx(&kv_full[g % KS], C::KV_BYTES);
-          __syncwarp();
+          mbar_arrive_expect_tx(&kv_full[g % KS], C::KV_BYTES);
           load_v(&kv_full[g % KS]);
-          __syncwarp();
-          if (lane == 0) mbar_arrive(&kv_full[g % KS]);
         }
       }
-      // Every load issued lands before the CTA exits, also when a role gave up
-      // and the loads were never consumed: the last phase armed on each K/V
-      // barrier and on each Q barrier (all earlier phases completed before
-      // their barrier was re-armed).
-      if (lane == 0) {
-        for (int j = armed > KS ? armed - KS : 0; j < armed; ++j)
-          mbar_wait(&kv_full[j % KS], (j / KS) & 1, nullptr, nullptr, p.wait_ns);
-        for (int j = qarmed > 2 ? qarmed - 2 : 0; j < qarmed; ++j)
-          mbar_wait(&q_full[j & 1], (j >> 1) & 1, nullptr, nullptr, p.wait_ns);
-      }
+      // Every load this thread issued lands before the CTA exits, also when a
+      // role gave up and the loads were never consumed: the last phase armed on
+      // each K/V barrier and on each Q barrier (all earlier phases completed
+      // before their barrier was re-armed).
+      for (int j = armed > KS ? armed - KS : 0; j < armed; ++j)
+        mbar_wait(&kv_full[j % KS], (j / KS) & 1, nullptr, nullptr, p.wait_ns);
+      for (int j = qarmed > 2 ? qarmed - 2 : 0; j < qarmed; ++j)
+        mbar_wait(&q_full[j & 1], (j >> 1) & 1, nullptr, nullptr, p.wait_ns);
     } else if (warp == 1 && lane == 0) {
       // ------------------------------------------------------------ MMA issuer
       constexpr uint32_t idesc_qk = make_idesc_f16(BF16, 128, C::BS, false, false);
@@ -776,10 +713,10 @@ struct MapKey {
   const void* k;
   const void* v;
   int64_t s[9];
-  int B, H, N, D, bf16, bn, gather;
+  int B, H, N, D, bf16, bn;
   bool operator==(const MapKey& o) const {
     if (q != o.q || k != o.k || v != o.v || B != o.B || H != o.H || N != o.N || D != o.D || bf16 != o.bf16 ||
-        bn != o.bn || gather != o.gather)
+        bn != o.bn)
       return false;
     for (int i = 0; i < 9; ++i)
       if (s[i] != o.s[i]) return false;
@@ -793,16 +730,13 @@ struct MapEntry {
 };
 constexpr int kMapCache = 8;
 
-// With `gather`, the K and V maps are the 2-D row maps of the row gathers
-// (k_rows / v_rows rows).
-int tensor_maps(const bsa_fwd_args* a, int D, bool bf16, int bn, bool gather, int64_t k_rows, int64_t v_rows,
-                CUtensorMap* mq, CUtensorMap* mk, CUtensorMap* mv) {
+int tensor_maps(const bsa_fwd_args* a, int D, bool bf16, int bn, CUtensorMap* mq, CUtensorMap* mk, CUtensorMap* mv) {
   thread_local MapEntry cache[kMapCache] = {};
   thread_local int next = 0;
   MapKey key{a->q.data, a->k.data, a->v.data,
              {a->q.stride_b, a->q.stride_h, a->q.stride_n, a->k.stride_b, a->k.stride_h, a->k.stride_n, a->v.stride_b,
               a->v.stride_h, a->v.stride_n},
-             a->B, a->H, a->N, D, bf16 ? 1 : 0, bn, gather ? 1 : 0};
+             a->B, a->H, a->N, D, bf16 ? 1 : 0, bn};
   for (int i = 0; i < kMapCache; ++i) {
     if (cache[i].used && cache[i].key == key) {
       *mq = cache[i].mq;
@@ -813,13 +747,8 @@ int tensor_maps(const bsa_fwd_args* a, int D, bool bf16, int bn, bool gather, in
   }
   int r;
   if ((r = make_tensor_map_4d(mq, a->q, a->B, a->H, a->N, D, bf16, 128))) return r;
-  if (gather) {
-    if ((r = make_tensor_map_rows(mk, a->k, k_rows, D, bf16))) return r;
-    if ((r = make_tensor_map_rows(mv, a->v, v_rows, D, bf16))) return r;
-  } else {
-    if ((r = make_tensor_map_4d(mk, a->k, a->B, a->H, a->N, D, bf16, bn))) return r;
-    if ((r = make_tensor_map_4d(mv, a->v, a->B, a->H, a->N, D, bf16, bn))) return r;
-  }
+  if ((r = make_tensor_map_4d(mk, a->k, a->B, a->H, a->N, D, bf16, bn))) return r;
+  if ((r = make_tensor_map_4d(mv, a->v, a->B, a->H, a->N, D, bf16, bn))) return r;
   MapEntry& e = cache[next];
   next = (next + 1) % kMapCache;
   e.key = key;
@@ -832,7 +761,7 @@ int tensor_maps(const bsa_fwd_args* a, int D, bool bf16, int bn, bool gather, in
 
 template <int D, int BN, bool BF16, bool PAIR>
 int launch_p(const bsa_fwd_args* a, cudaStream_t st, const void* q_perm, int perm_dtype, int select,
-             uint32_t test_wait_us, const void* kv_perm) {
+             uint32_t test_wait_us) {
   using C = TcpCfg<D, BN, PAIR>;
   auto kern = attn_tcp_kernel<D, BN, BF16, PAIR>;
   // The setmaxnreg split needs the launch to hold at least the sum of the
@@ -853,21 +782,10 @@ int launch_p(const bsa_fwd_args* a, cudaStream_t st, const void* q_perm, int per
     BSA_CUDA_CHECK(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM));
     smem_set[dev].store(true, std::memory_order_release);
   }
-  int64_t k_rb = 0, k_rh = 0, k_rows = 0, v_rb = 0, v_rh = 0, v_rows = 0;
-  if (kv_perm && !(rows_gatherable(a->k, a->B, a->H, a->N, &k_rb, &k_rh, &k_rows) &&
-                   rows_gatherable(a->v, a->B, a->H, a->N, &v_rb, &v_rh, &v_rows)))
-    return BSA_ERR_UNSUPPORTED;
   CUtensorMap mq, mk, mv;
   int r;
-  if ((r = tensor_maps(a, D, BF16, BN, kv_perm != nullptr, k_rows, v_rows, &mq, &mk, &mv))) return r;
+  if ((r = tensor_maps(a, D, BF16, BN, &mq, &mk, &mv))) return r;
   TcpParams p;
-  p.kv_perm = kv_perm;
-  p.k_rb = k_rb;
-  p.k_rh = k_rh;
-  p.v_rb = v_rb;
-  p.v_rh = v_rh;
-  p.k_rows = static_cast<int>(k_rows);
-  p.v_rows = static_cast<int>(v_rows);
   p.tile_ptr = a->plan.tile_ptr;
   p.tile_col = a->plan.tile_col;
   p.tile_order = a->plan.tile_order;
@@ -916,8 +834,7 @@ int launch_p(const bsa_fwd_args* a, cudaStream_t st, const void* q_perm, int per
 
 }  // namespace
 
-int launch_attn_tcp(const bsa_fwd_args* a, cudaStream_t st, const void* q_perm, int perm_dtype,
-                    const void* kv_perm) {
+int launch_attn_tcp(const bsa_fwd_args* a, cudaStream_t st, const void* q_perm, int perm_dtype) {
   const bool bf16 = a->dtype == BSA_DTYPE_BF16;
   const int bn = a->plan.block;
   // an armed timeout test applies to this forward (both BLOCK 64 launches)
@@ -927,14 +844,14 @@ int launch_attn_tcp(const bsa_fwd_args* a, cudaStream_t st, const void* q_perm, 
 #define BSA_TCP_CASE(D_, BN_)                                                                     \
   if (a->D == D_ && bn == BN_) {                                                                  \
     if constexpr (BN_ == 128)                                                                     \
-      return bf16 ? launch_p<D_, BN_, true, false>(a, st, q_perm, perm_dtype, 0, tw, kv_perm)                  \
-                  : launch_p<D_, BN_, false, false>(a, st, q_perm, perm_dtype, 0, tw, kv_perm);                \
+      return bf16 ? launch_p<D_, BN_, true, false>(a, st, q_perm, perm_dtype, 0, tw)                  \
+                  : launch_p<D_, BN_, false, false>(a, st, q_perm, perm_dtype, 0, tw);                \
     else {                                                                                        \
-      int r_ = bf16 ? launch_p<D_, BN_, true, true>(a, st, q_perm, perm_dtype, 1, tw, kv_perm)                 \
-                    : launch_p<D_, BN_, false, true>(a, st, q_perm, perm_dtype, 1, tw, kv_perm);               \
+      int r_ = bf16 ? launch_p<D_, BN_, true, true>(a, st, q_perm, perm_dtype, 1, tw)                 \
+                    : launch_p<D_, BN_, false, true>(a, st, q_perm, perm_dtype, 1, tw);               \
       if (r_) return r_;                                                                          \
-      return bf16 ? launch_p<D_, BN_, true, false>(a, st, q_perm, perm_dtype, 2, tw, kv_perm)                  \
-                  : launch_p<D_, BN_, false, false>(a, st, q_perm, perm_dtype, 2, tw, kv_perm);                \
+      return bf16 ? launch_p<D_, BN_, true, false>(a, st, q_perm, perm_dtype, 2, tw)                  \
+                  : launch_p<D_, BN_, false, false>(a, st, q_perm, perm_dtype, 2, tw);                \
     }                                                                                             \
   }
   BSA_TCP_CASE(64, 64)

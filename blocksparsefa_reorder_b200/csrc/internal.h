@@ -38,19 +38,12 @@ int launch_attn_simt(const bsa_fwd_args* a, cudaStream_t st);
 // over a [B, H, N, D] 16-bit tensor, box 64 x rows, 128-byte swizzle.
 bool attn_tc_supported(const bsa_fwd_args* a);
 int make_tensor_map_4d(CUtensorMap* m, const bsa_tensor4d& t, int B, int H, int N, int D, bool bf16, int rows);
-// The row view of a [B, H, N, D] tensor for row gathers: true when its b and
-// h strides are whole multiples of its row stride (then row (b, h, n) = b*rb +
-// h*rh + n, `rows` rows in all, below 2^31), and the 2-D map over those rows.
-bool rows_gatherable(const bsa_tensor4d& t, int B, int H, int N, int64_t* rb, int64_t* rh, int64_t* rows);
-int make_tensor_map_rows(CUtensorMap* m, const bsa_tensor4d& t, int64_t rows, int D, bool bf16);
 
 // attn_tcp.cu: the persistent tcgen05 attention forward
 // q_perm (optional, bsa_index_dtype perm_dtype): gather Q rows from and
-// scatter O / lse rows to q_perm[row] inside the kernel; kv_perm (optional):
-// gather K / V rows through it inside the kernel (both tensors must pass
-// rows_gatherable).
+// scatter O / lse rows to q_perm[row] inside the kernel.
 int launch_attn_tcp(const bsa_fwd_args* a, cudaStream_t st, const void* q_perm = nullptr,
-                    int perm_dtype = BSA_INDEX_I64, const void* kv_perm = nullptr);
+                    int perm_dtype = BSA_INDEX_I64);
 // Arms the timeout test for the next launch_attn_tcp call (see
 // bsa_test_arm_wait_timeout).
 int arm_test_wait_timeout(uint32_t wait_us);

@@ -155,12 +155,7 @@ BSA_API int bsa_build_plan_noalloc(const uint8_t* mask, int64_t stride_b, int64_
  * Replaces _attn_fwd_block_sparse (triton_kernels/BlockSparse_Naive.py:68-125)
  * as launched at BlockSparseTriton_Naive.py:142-156: o = softmax over kept
  * blocks of (q k^T * sm_scale) v; rows that keep no block give o = 0 and
- * lse = -inf.  Key blocks outside a row's kept set contribute exactly zero,
- * with one condition at BLOCK 64 on the tensor-core path: a 128-row tile
- * reads every key block either of its two block rows keeps and multiplies
- * the other row's zero probabilities with that block's V, so V must be
- * finite in blocks kept by a row's partner row (NaN / Inf in blocks no row
- * of the tile keeps are never read). */
+ * lse = -inf. */
 BSA_API int bsa_fwd(const bsa_fwd_args* args, void* stream);
 
 /* Row gather / scatter along N for every (b, h); D = elements per row:
@@ -204,11 +199,8 @@ BSA_API int bsa_blockmask_from_coords(const int64_t* rows, const int64_t* cols, 
  * be NULL (identity).  Mirrors the timed loop of
  * BlockSparseTriton_Naive.py:129-161 and the fused kernel
  * triton_kernels/BlockSparse_Fused.py:115-223.  On the tcgen05 path the
- * query gather, the k / v row gathers (TMA gathers of four rows) and the o /
- * lse scatter all run inside the attention kernel, with no workspace for
- * them, when k and v have a row view (b and h strides multiples of the row
- * stride, as in contiguous [B,H,N,D]); other layouts permute k and v into the
- * workspace first.  The SIMT path permutes every tensor.
+ * query gather and the o / lse scatter run inside the attention kernel and
+ * k, v are permuted into the workspace; the SIMT path permutes every tensor.
  * With `args->err_flag` set, both permutations are first checked on the
  * device (values outside [0, N) set BSA_DEVERR_PERM_RANGE, repeated values
  * BSA_DEVERR_PERM_DUP); the workspace then also holds the check's bits, so

@@ -71,29 +71,6 @@ def test_fwd_validation_on_host(kw, status):
     assert L.bsa_fwd(ctypes.byref(a), None) == status
 
 
-def test_reordered_workspace_sizes():
-    """The reordered forward's workspace: none on the tensor-core path when k
-    and v have a row view (K / V rows are gathered inside the kernel); k' and
-    v' for a [B, N, H, D] layout (permuted beforehand); the permutation
-    check's bits when an error word is given."""
-    L = _lib.lib()
-    n = ctypes.c_size_t()
-    a = _args()  # contiguous [1, 2, 256, 64] bf16
-    assert L.bsa_fwd_reordered_workspace_bytes(ctypes.byref(a), ctypes.byref(n)) == 0
-    assert n.value == 0
-    a.err_flag = 0x2000
-    assert L.bsa_fwd_reordered_workspace_bytes(ctypes.byref(a), ctypes.byref(n)) == 0
-    assert n.value == 256  # ceil(256 / 32) words, rounded up to 256 bytes
-    a = _args()
-    for t in ("k", "v"):  # [B, N, H, D] memory viewed as [B, H, N, D]
-        setattr(a, t, _lib.Tensor4d(0x1000, 256 * 2 * 64, 64, 2 * 64))
-    assert L.bsa_fwd_reordered_workspace_bytes(ctypes.byref(a), ctypes.byref(n)) == 0
-    assert n.value == 2 * 2 * 256 * 64 * 2
-    a = _args(dtype=_lib.DTYPE_F32)  # SIMT path: q', k', v', o' (+ lse' when asked)
-    assert L.bsa_fwd_reordered_workspace_bytes(ctypes.byref(a), ctypes.byref(n)) == 0
-    assert n.value == 4 * 2 * 256 * 64 * 4
-
-
 def test_fwd_null_pointers_rejected():
     L = _lib.lib()
     a = _args()
@@ -117,12 +94,12 @@ def test_other_entry_points_validate_on_host():
     assert L.bsa_test_arm_wait_timeout(3_000_000) == 1                                # above 2 s: refused
     size = ctypes.c_size_t()
     assert L.bsa_fwd_reordered_workspace_bytes(ctypes.byref(_args()), ctypes.byref(size)) == 0
-    # fused tcgen05 forward: Q, K, V and O all go through the permutations in-kernel
-    assert size.value == 0
+    # fused tcgen05 forward: k', v' of 1*2*256*64 bf16 each (Q and O go through the permutation in-kernel)
+    assert size.value == 2 * 2 * 256 * 64 * 2
     assert L.bsa_fwd_reordered_workspace_bytes(ctypes.byref(_args(kernel=1)), ctypes.byref(size)) == 0
     # SIMT forward: q', k', v', o' (lse not requested)
     assert size.value == 4 * 2 * 256 * 64 * 2
-    a = _args(kernel=1)  # the SIMT path permutes into the workspace
+    a = _args()
     assert L.bsa_fwd_reordered(ctypes.byref(a), None, 0x1000, 1, None, 0, None) == 9   # workspace missing
     assert L.bsa_fwd_reordered(ctypes.byref(_args(kernel=1)), 0x1000, None, 1, None, 0, None) == 9
     assert L.bsa_fwd_reordered(ctypes.byref(a), 0x1000, None, 7, 0x1000, 1 << 30, None) == 3  # perm dtype
