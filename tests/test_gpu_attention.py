@@ -120,13 +120,14 @@ def test_permuted_path_matches_oracle(dev, dtype):
 
 @pytest.mark.parametrize("which", ["q", "kv", "both"])
 @pytest.mark.parametrize("D,block,N,idx", [(128, 128, 1024, torch.int64), (64, 64, 64 * 13, torch.int32),
-                                           (128, 64, 64 * 9, torch.int64)])
+                                           (128, 64, 64 * 9, torch.int64), (128, 128, 1000, torch.int32),
+                                           (64, 64, 64 * 7 + 40, torch.int64)])
 def test_fused_permutation(dev, which, D, block, N, idx):
     """The reordered forward on the tcgen05 path gathers Q rows and scatters
     O / lse rows through q_perm inside the attention kernel (K and V are
     permuted beforehand): every combination of permutations, BLOCK 64 with a
-    partial last 128-row tile, int32 and int64 permutations, NaN-prefilled
-    outputs, against the oracle's reordered attention (BlockSparse_Fused.py
+    partial last 128-row tile, N not a multiple of BLOCK (a partial last key
+    block), int32 and int64 permutations, NaN-prefilled outputs, against the oracle's reordered attention (BlockSparse_Fused.py
     semantics: mask in the new order, output in the original order)."""
     B, H = 2, 2
     nb = (N + block - 1) // block
@@ -248,6 +249,27 @@ def test_strided_bnhd_layout(dev):
     o = block_sparse_attention(q, k, v, torch.from_numpy(mask).to(dev), kernel="tcgen05")
     ref, _ = _oracle(q, k, v, mask, block)
     assert _maxerr(o, ref) <= TOL_16
+
+
+@pytest.mark.parametrize("block", [128, 64])
+def test_permutations_on_strided_layout(dev, block):
+    """q, k, v as [B, N, H, D] memory viewed as [B, H, N, D] with both
+    permutations: K / V are permuted into the workspace (contiguous), Q is
+    gathered inside the kernel through its own strides and O / lse scattered
+    through q_perm."""
+    B, H, N, D = 2, 3, 1024, 128
+    mask = _rand_mask(N // block, 0.4, seed=33, shape=(1, H))
+    base = [torch.randn(B, N, H, D, generator=torch.Generator().manual_seed(50 + i)).to(torch.bfloat16).to(dev)
+            for i in range(3)]
+    q, k, v = (t.permute(0, 2, 1, 3) for t in base)
+    g = torch.Generator().manual_seed(51)
+    qp = torch.randperm(N, generator=g).to(dev)
+    kp = torch.randperm(N, generator=g).to(dev)
+    o, lse = block_sparse_attention(q, k, v, torch.from_numpy(mask).to(dev), q_perm=qp, kv_perm=kp, return_lse=True,
+                                    kernel="tcgen05", check_errors=True)
+    ref, ref_lse = _oracle(q, k, v, mask, block, qp, kp)
+    assert _maxerr(o, ref) <= TOL_16
+    assert np.abs(lse.cpu().numpy() - ref_lse).max() <= TOL_LSE
 
 
 def test_partial_last_tile(dev):
