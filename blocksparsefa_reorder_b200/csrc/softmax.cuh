@@ -8,18 +8,22 @@
 // only that 2^(s*scale - m) stays finite: P is rounded to bf16 / fp16 relative
 // to its own magnitude and O, l accumulate in fp32, both with 8-bit exponents.
 // So here m_run is the exact max of the row's FIRST kept block only; later
-// blocks reuse it, and only when a block's sum exceeds kRefSlack (a score more
-// than ~32 above m_run in log2 units, or an overflow) is the block redone with
-// the exact max and O, l scaled by 2^(m_old - m_new).  lse = m_run + log2(l)
-// is exact either way.  This removes the per-block max (a 128-deep fmax
-// chain) from the common path.
+// blocks reuse it, and only when a block's sum exceeds the slack is the block
+// redone with the exact max and O, l scaled by 2^(m_old - m_new).  The slack
+// bounds every single p as well: 2^32 for bf16 (8-bit exponent, like fp32);
+// 2^15 for fp16, whose largest finite value is 65504, so no p of a kept
+// block rounds to infinity.  lse = m_run + log2(l) is exact either way.  This
+// removes the per-block max (a 128-deep fmax chain) from the common path.
 #pragma once
 
 #include "common.cuh"
 
 namespace bsa {
 
-constexpr float kRefSlack = 4294967296.f;  // 2^32
+template <bool BF16>
+__host__ __device__ constexpr float ref_slack() {
+  return BF16 ? 4294967296.f /* 2^32 */ : 32768.f /* 2^15 */;
+}
 
 // Max of a row's BN scores (fp32 bits), as a tree of 8 independent chains.
 template <int BN>
@@ -94,7 +98,7 @@ __device__ __forceinline__ float softmax_block(const uint32_t (&sr)[BN], uint32_
   if (m_run == -INFINITY) m_run = row_max<BN>(sr) * scale_log2;
   float ls = exp_block<BN, BF16>(sr, pr, scale_log2, -m_run);
   float alpha = 1.f;
-  if (!(ls <= kRefSlack)) {
+  if (!(ls <= ref_slack<BF16>())) {
     const float m_new = fmaxf(m_run, row_max<BN>(sr) * scale_log2);
     alpha = ex2_approx(m_run - m_new);
     l_run *= alpha;

@@ -366,23 +366,25 @@ def test_many_tiles_per_cta(dev, D, block):
         assert torch.equal(o, first[0]) and torch.equal(lse, first[1])
 
 
+@pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float16])
 @pytest.mark.parametrize("D,block", [(64, 64), (128, 64), (64, 128), (128, 128)])
-def test_reference_point_guard(dev, D, block):
+def test_reference_point_guard(dev, D, block, dtype):
     """The kernels take a row's softmax reference point from its first kept
-    block and redo a block with the exact max only when its sum overflows
-    the slack: keys of one later block scaled by 30 force that path (scores
-    ~40 log2 units above the reference), and an earlier block scaled down
-    makes the first reference point low.  Checked against the float64
-    oracle, O and lse."""
+    block and redo a block with the exact max only when its sum leaves the
+    slack: keys of one later block scaled by 30 force that path (scores ~40
+    log2 units above the reference: past fp16's range for P without the redo),
+    and an earlier block scaled down makes the first reference point low.
+    Checked against the float64 oracle, O and lse, with finite outputs."""
     B, H, N = 1, 2, 1024
     nb = N // block
     mask = _rand_mask(nb, 0.6, seed=D + block + 3, shape=(1, H))
     mask[..., :, nb - 2] = True
-    q, k, v = _qkv(B, H, N, D, torch.bfloat16, seed=D + block, dev=dev)
+    q, k, v = _qkv(B, H, N, D, dtype, seed=D + block, dev=dev)
     k[:, :, (nb - 2) * block:(nb - 1) * block] *= 30
     k[:, :, :block] *= 0.1
     o, lse = block_sparse_attention(q, k, v, torch.from_numpy(mask).to(dev), return_lse=True, kernel="tcgen05",
                                     check_errors=True)
+    assert torch.isfinite(o.float()).all()
     ref, ref_lse = _oracle(q, k, v, mask, block)
     assert _maxerr(o, ref) <= TOL_16
     lv = lse.cpu().numpy()
