@@ -124,8 +124,10 @@ def _pairing_mask(nb, H, p, seed):
 @pytest.mark.parametrize("dtype", [torch.float16, torch.bfloat16])
 @pytest.mark.parametrize("D", [64, 128])
 def test_block64_paired_form(dev, dtype, D):
-    """BLOCK 64 with tiles averaging > 32 kept key blocks, so the kernel form
-    that takes a tile's entries two at a time (128-key steps) runs: odd entry
+    """BLOCK 64 with tiles averaging > 32 kept key blocks, so the dense-plan
+    kernel form runs (D 128: each 64-row query block over pairs of its own kept
+    key blocks, transposed; D 64: the 128-row tile over pairs of its entries):
+    odd entry
     counts (the repeated, masked second entry), blocks kept by only one of a
     tile's two block rows, rows with disjoint kept sets, a row keeping only the
     partial last key block (N % 64 = 23) and a partial last 128-row tile (odd
@@ -213,3 +215,61 @@ def test_repeated_permutation_value_flagged(dev, which):
     good = torch.randperm(N).to(dev)
     kw = {"q_perm": good} if which == "q" else {"kv_perm": good}
     block_sparse_attention(q, k, v, torch.from_numpy(mask).to(dev), kernel="tcgen05", check_errors=True, **kw)
+
+
+@pytest.mark.parametrize("dtype", [torch.float16, torch.bfloat16])
+def test_block64_dense_reference_point_guard(dev, dtype):
+    """The dense BLOCK 64 form at D 128 takes each query's reference point
+    from the column max of its first pair and redoes a pair (column max,
+    O^T and row sums rescaled, decided by a vote across the warpgroup) when a
+    score leaves the slack: one key block scaled by 30 (~40 log2 units above
+    the reference, past fp16's range for P without the redo), an early block
+    scaled down.  O (finite) and lse against the float64 oracle."""
+    B, H, block, D = 1, 2, 64, 128
+    N = 64 * 60
+    nb = N // block
+    rng = np.random.default_rng(17)
+    mask = rng.random((1, H, nb, nb)) < 0.8
+    mask[..., np.arange(nb), np.arange(nb)] = True
+    mask[..., :, nb - 3] = True
+    g = torch.Generator(device="cpu").manual_seed(18)
+    q, k, v = (torch.randn(B, H, N, D, generator=g).to(dtype).to(dev) for _ in range(3))
+    k[:, :, (nb - 3) * block:(nb - 2) * block] *= 30
+    k[:, :, :block] *= 0.1
+    plan = BlockSparsePlan(torch.from_numpy(mask).to(dev), block)
+    assert plan.nnz_entries() >= PAIR_MIN_ENTRIES * plan.mask_b * plan.mask_h * plan.tiles_per_row
+    o, lse = block_sparse_attention(q, k, v, plan=plan, return_lse=True, kernel="tcgen05", check_errors=True)
+    assert torch.isfinite(o.float()).all()
+    f = lambda t: t.float().cpu().numpy()  # noqa: E731
+    ref, ref_lse = OA.dense_masked_attention(f(q), f(k), f(v), mask, block)
+    assert np.abs(f(o) - ref).max() <= TOL_16
+    lv = lse.cpu().numpy()
+    fin = np.isfinite(ref_lse)
+    assert np.array_equal(np.isfinite(lv), fin)
+    assert np.abs(lv[fin] - ref_lse[fin]).max() <= TOL_LSE * max(1.0, float(np.abs(ref_lse[fin]).max()) / 8)
+
+
+def test_block64_dense_wait_timeout(dev):
+    """The bounded-wait timeout on the dense BLOCK 64 form: one softmax warp
+    of CTA 0 withholds its first arrival (test hook, 1 ms limit); the host sees
+    the timeout and the next forwards, including the one that reuses the
+    work-counter slot, equal the result before."""
+    from blocksparsefa_reorder_b200 import _lib
+
+    B, H, block, D = 1, 4, 64, 128
+    N = 64 * 64
+    nb = N // block
+    rng = np.random.default_rng(19)
+    mask = rng.random((1, 1, nb, nb)) < 0.7
+    mask[..., np.arange(nb), np.arange(nb)] = True
+    g = torch.Generator(device="cpu").manual_seed(20)
+    q, k, v = (torch.randn(B, H, N, D, generator=g).to(torch.bfloat16).to(dev) for _ in range(3))
+    plan = BlockSparsePlan(torch.from_numpy(mask).to(dev), block)
+    assert plan.nnz_entries() >= PAIR_MIN_ENTRIES * plan.tiles_per_row
+    good = block_sparse_attention(q, k, v, plan=plan, kernel="tcgen05", check_errors=True)
+    assert _lib.lib().bsa_test_arm_wait_timeout(1000) == 0
+    with pytest.raises(RuntimeError, match="device wait timed out"):
+        block_sparse_attention(q, k, v, plan=plan, kernel="tcgen05", check_errors=True)
+    for _ in range(65):
+        o = block_sparse_attention(q, k, v, plan=plan, kernel="tcgen05", check_errors=True)
+        assert torch.equal(o, good)
