@@ -694,8 +694,6 @@ __global__ void __launch_bounds__(kThreadsP, 1)
   }
 }
 
-}  // namespace
-
 int sm_count() {
   static int count[64];
   int dev = 0;
@@ -760,8 +758,6 @@ int tensor_maps(const bsa_fwd_args* a, int D, bool bf16, int bn, CUtensorMap* mq
   e.used = true;
   return BSA_OK;
 }
-
-namespace {
 
 template <int D, int BN, bool BF16, bool PAIR>
 int launch_p(const bsa_fwd_args* a, cudaStream_t st, const void* q_perm, int perm_dtype, int select,
@@ -858,16 +854,9 @@ int launch_attn_tcp(const bsa_fwd_args* a, cudaStream_t st, const void* q_perm, 
                   : launch_p<D_, BN_, false, false>(a, st, q_perm, perm_dtype, 2, tw);                \
     }                                                                                             \
   }
-  // BLOCK 64 at D 128: dense plans run the transposed per-query-block form
-  // (attn_tt.cu) instead of the paired one, sparse plans the single form
-  if (a->D == 128 && bn == 64) {
-    int r_ = launch_attn_tt(a, st, q_perm, perm_dtype, tw);
-    if (r_) return r_;
-    return bf16 ? launch_p<128, 64, true, false>(a, st, q_perm, perm_dtype, 2, tw)
-                : launch_p<128, 64, false, false>(a, st, q_perm, perm_dtype, 2, tw);
-  }
   BSA_TCP_CASE(64, 64)
   BSA_TCP_CASE(64, 128)
+  BSA_TCP_CASE(128, 64)
   BSA_TCP_CASE(128, 128)
 #undef BSA_TCP_CASE
   return BSA_ERR_UNSUPPORTED;

@@ -47,16 +47,6 @@ int launch_attn_tcp(const bsa_fwd_args* a, cudaStream_t st, const void* q_perm =
 // Arms the timeout test for the next launch_attn_tcp call (see
 // bsa_test_arm_wait_timeout).
 int arm_test_wait_timeout(uint32_t wait_us);
-// Number of SMs of the current device.
-int sm_count();
-// The Q, K, V tensor maps of a forward (Q boxes of 128 rows, K / V boxes of
-// `bn` rows), cached per thread across calls with the same tensors.
-int tensor_maps(const bsa_fwd_args* a, int D, bool bf16, int bn, CUtensorMap* mq, CUtensorMap* mk, CUtensorMap* mv);
-
-// attn_tt.cu: BLOCK 64, D 128, dense plans: 64-row query blocks computed in
-// the transposed orientation (see the file).  select as for attn_tcp's forms:
-// run only if the plan averages at least kPairMinEntries kept blocks per tile.
-int launch_attn_tt(const bsa_fwd_args* a, cudaStream_t st, const void* q_perm, int perm_dtype, uint32_t test_wait_us);
 
 
 }  // namespace bsa

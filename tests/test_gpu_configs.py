@@ -124,10 +124,8 @@ def _pairing_mask(nb, H, p, seed):
 @pytest.mark.parametrize("dtype", [torch.float16, torch.bfloat16])
 @pytest.mark.parametrize("D", [64, 128])
 def test_block64_paired_form(dev, dtype, D):
-    """BLOCK 64 with tiles averaging > 32 kept key blocks, so the dense-plan
-    kernel form runs (D 128: each 64-row query block over pairs of its own kept
-    key blocks, transposed; D 64: the 128-row tile over pairs of its entries):
-    odd entry
+    """BLOCK 64 with tiles averaging > 32 kept key blocks, so the kernel form
+    that takes a tile's entries two at a time (128-key steps) runs: odd entry
     counts (the repeated, masked second entry), blocks kept by only one of a
     tile's two block rows, rows with disjoint kept sets, a row keeping only the
     partial last key block (N % 64 = 23) and a partial last 128-row tile (odd
@@ -219,12 +217,12 @@ def test_repeated_permutation_value_flagged(dev, which):
 
 @pytest.mark.parametrize("dtype", [torch.float16, torch.bfloat16])
 def test_block64_dense_reference_point_guard(dev, dtype):
-    """The dense BLOCK 64 form at D 128 takes each query's reference point
-    from the column max of its first pair and redoes a pair (column max,
-    O^T and row sums rescaled, decided by a vote across the warpgroup) when a
-    score leaves the slack: one key block scaled by 30 (~40 log2 units above
-    the reference, past fp16's range for P without the redo), an early block
-    scaled down.  O (finite) and lse against the float64 oracle."""
+    """The paired BLOCK 64 form (dense plans) takes each row's reference point
+    from the exact max of its first kept step and redoes a step with the exact
+    max (O and the row sum rescaled) when a score leaves the slack: one key
+    block scaled by 30 (~40 log2 units above the reference, past fp16's range
+    for P without the redo), an early block scaled down.  O (finite) and lse
+    against the float64 oracle."""
     B, H, block, D = 1, 2, 64, 128
     N = 64 * 60
     nb = N // block
@@ -250,7 +248,7 @@ def test_block64_dense_reference_point_guard(dev, dtype):
 
 
 def test_block64_dense_wait_timeout(dev):
-    """The bounded-wait timeout on the dense BLOCK 64 form: one softmax warp
+    """The bounded-wait timeout on the paired BLOCK 64 form: one softmax warp
     of CTA 0 withholds its first arrival (test hook, 1 ms limit); the host sees
     the timeout and the next forwards, including the one that reuses the
     work-counter slot, equal the result before."""
