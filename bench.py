@@ -10,8 +10,12 @@ token permutation; the query permutation is applied inside the attention
 kernel).  As in the reference's timed loop (BlockSparseTriton_Naive.py:
 131-161 reuses one block mask for every iteration), the plan is built once per
 mask before timing; the plan build is timed on its own and a second number
-rebuilds it every step.  Each step is replayed from a CUDA graph of the call
-(the same kernels the eager call launches, without per-step host work).
+rebuilds it every step.  The steps are replayed from CUDA graphs of the call
+(the same kernels the eager call launches, without per-step host work): a
+graph of 8 (or more, whole rotations over the input copies) forwards back to
+back, then single-forward graphs for the remainder, so that exactly K
+forwards run; the attention kernel's own time is taken from events around
+single-forward replays.
 Inputs are resident in HBM when timing starts; when one rank's inputs would
 fit in L2 the steps rotate over several input copies so that every step reads
 from DRAM.  K steps are timed with CUDA events between a barrier + synchronize
@@ -234,9 +238,12 @@ def algorithmic_bytes(wl, units: int) -> float:
 
 class Runner:
     """A workload's units [lo, hi) resident on this GPU, its plan built once,
-    and a CUDA graph of one forward per input copy."""
+    a CUDA graph of one forward per input copy, and one graph of ``group``
+    forwards back to back (whole rotations over the copies, at least
+    ``batch``), which the timed loops replay so that consecutive forwards are
+    not separated by a graph launch each."""
 
-    def __init__(self, wl, dev, lo, hi, seed=None, copies=None, graphs=True, kernel="auto"):
+    def __init__(self, wl, dev, lo, hi, seed=None, copies=None, graphs=True, kernel="auto", batch=8):
         import torch
 
         from blocksparsefa_reorder_b200 import BlockSparsePlan
@@ -257,6 +264,7 @@ class Runner:
             self.sets.append((q.clone(), k.clone(), v.clone(), torch.empty_like(q)))
         self.footprint = per_copy * copies
         self.graphs = []
+        self.batched, self.group = None, 1
         # warm the host-side caches and the kernels once per copy, then capture
         for s in self.sets:
             self.forward(s)
@@ -267,6 +275,12 @@ class Runner:
                 with torch.cuda.graph(g):
                     self.forward(s)
                 self.graphs.append(g)
+            self.group = copies * max(1, math.ceil(batch / copies))
+            self.batched = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(self.batched):
+                for i in range(self.group):
+                    self.forward(self.sets[i % copies])
+            self.batched.replay()  # first launch (graph upload) outside any timed region
             torch.cuda.synchronize(dev)
 
     def forward(self, s):
@@ -282,6 +296,14 @@ class Runner:
         else:
             self.forward(self.sets[i % len(self.sets)])
 
+    def run_steps(self, n):
+        """Exactly n forwards: whole replays of the batched graph, then single ones."""
+        full, rest = divmod(n, self.group) if self.batched is not None else (0, n)
+        for _ in range(full):
+            self.batched.replay()
+        for i in range(rest):
+            self.step(i)
+
     @property
     def flops(self):
         return self.wl.flops * self.units / (self.wl.B * self.wl.H)
@@ -292,6 +314,7 @@ class Runner:
 
     def release(self):
         self.graphs = []
+        self.batched = None
         self.sets = []
 
 
@@ -319,6 +342,22 @@ def time_steps(run, steps, stream, world, per_step_events=False):
     barrier(world)
     ms = start.elapsed_time(end) / steps
     return max_over_ranks(ms, world), [a.elapsed_time(b) for a, b in evs]
+
+
+def time_block(run_n, steps, stream, world):
+    """Time ``run_n(steps)`` (all steps issued at once) between barrier +
+    synchronize; ms per step, max over ranks."""
+    import torch
+
+    barrier(world)
+    torch.cuda.synchronize()
+    start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    start.record(stream)
+    run_n(steps)
+    end.record(stream)
+    torch.cuda.synchronize()
+    barrier(world)
+    return max_over_ranks(start.elapsed_time(end) / steps, world)
 
 
 def time_plan(plan, mask, stream, reps=20):
@@ -486,8 +525,7 @@ def measure_config(name, dev, peaks, steps=10, warmup=3, kernel="auto"):
     run = Runner(wl, dev, 0, units, kernel=kernel)
     for i in range(warmup):
         run.step(i)
-    step_ms, evs = time_steps(run.step, steps, stream, 1, per_step_events=True)
-    kern_ms = statistics.mean(evs)
+    kernel_call, extra = run.step, None
     if run.kp is not None:
         # the attention kernel alone: K and V already in the new order, the
         # query permutation (fused into the kernel) still applied
@@ -505,9 +543,19 @@ def measure_config(name, dev, peaks, steps=10, warmup=3, kernel="auto"):
             call()
         for _ in range(warmup):
             g.replay()
-        _, evs = time_steps(lambda i: g.replay(), steps, stream, 1, per_step_events=True)
-        kern_ms = statistics.mean(evs)
-        del g, k2, v2
+        kernel_call, extra = (lambda i: g.replay()), (g, k2, v2)
+    # the kernel alone first, then the whole steps, with the SM clock of each
+    with ClockSampler(dev.index if dev.index is not None else 0, period_s=0.001) as clk:
+        t0 = time.time()
+        _, evs = time_steps(kernel_call, steps, stream, 1, per_step_events=True)
+        t1 = time.time()
+        step_ms = time_block(run.run_steps, steps, stream, 1)
+        t2 = time.time()
+    kern_ms = statistics.mean(evs)
+    ck, cs = clk.summary(t0, t1, "kernel"), clk.summary(t1, t2, "step")
+    clocks = {"kernel_sm_mhz": ck["sm_mhz"], "step_sm_mhz": cs["sm_mhz"],
+              "reasons": sorted(set(ck["reasons"]) | set(cs["reasons"]))}
+    del extra
     # correctness spot check of the whole step's output
     run.step(0)
     torch.cuda.synchronize()
@@ -540,6 +588,7 @@ def measure_config(name, dev, peaks, steps=10, warmup=3, kernel="auto"):
         "algorithmic_bytes": nbytes, "algorithmic_flops": flops,
         "max_abs_err": err, "err_check": "fp64 masked softmax on the host, query blocks %s of (b,h) units 0 and %d"
                                          % (qbs, units - 1),
+        "clocks": clocks,
     }
     run.release()
     del run
@@ -564,12 +613,19 @@ def run_ours(args):
     units_total = wl.B * wl.H
     scaling = scaling_of(world, args.scaling)
     strong = scaling == "strong"
-    ranges = sharding.partition_units(units_total, world) if strong else [(0, units_total)] * world
+    if args.units:
+        # a smaller case of the same kernel (ncu captures): the first U (b, h)
+        # units of the workload on every rank
+        strong, scaling = False, "weak"
+        ranges = [(0, min(args.units, units_total))] * world
+    else:
+        ranges = sharding.partition_units(units_total, world) if strong else [(0, units_total)] * world
     lo, hi = ranges[rank]
     gather = strong and wl.name == "longctx"
     run = Runner(wl, dev, lo, hi, seed=None if strong or world == 1 else wl.seed + 1000 * rank,
                  graphs=not gather, kernel=args.kernel)
     per_rank_flops = run.flops
+    job_flops = wl.flops if strong else per_rank_flops * world
 
     if gather:
         # long context: each rank's heads in two halves; a half's O goes to
@@ -597,17 +653,26 @@ def run_ours(args):
     else:
         step = run.step
 
+    def run_n(n):
+        if gather:
+            for i in range(n):
+                step(i)
+        else:
+            run.run_steps(n)
+
     for i in range(args.warmup):
         step(i)
     torch.cuda.synchronize()
     # the timed region follows the warm-up directly (clocks at their burst
-    # level); NVML is sampled every millisecond through it
+    # level); NVML is sampled every millisecond through it.  The attention
+    # kernel's own time comes from events around single steps right after.
     with ClockSampler(local, period_s=0.001) as clk:
         t_wall0 = time.time()
-        ms_step, evs = time_steps(step, args.steps, stream, world, per_step_events=True)
+        ms_step = time_block(run_n, args.steps, stream, world)
         t_wall1 = time.time()
+        _, evs = time_steps(step, args.steps, stream, world, per_step_events=True)
     kern_ms = max_over_ranks(statistics.mean(evs), world)
-    value = wl.flops * (1 if strong else world) / (ms_step * 1e-3) / 1e12
+    value = job_flops / (ms_step * 1e-3) / 1e12
     clocks = clk.summary(t_wall0, t_wall1, "timed region")
 
     # the same steps after ~sustained_seconds of continuous load (power cap
@@ -617,16 +682,16 @@ def run_ours(args):
         t_one, _ = time_steps(step, 3, stream, world)
         n_load = max(1, int(args.sustained_seconds * 1e3 / max(t_one, 1e-3)))
         with ClockSampler(local, period_s=0.005) as clk_s:
-            for i in range(n_load):
-                step(i)
+            run_n(n_load)
             torch.cuda.synchronize()
             ts0 = time.time()
-            ms_s, evs_s = time_steps(step, args.steps, stream, world, per_step_events=True)
+            ms_s = time_block(run_n, args.steps, stream, world)
             ts1 = time.time()
+            _, evs_s = time_steps(step, args.steps, stream, world, per_step_events=True)
         kern_s = max_over_ranks(statistics.mean(evs_s), world)
         sus_peak = float(peaks.get("bf16_tflops_sustained", FALLBACK_PEAKS["bf16_tflops_sustained"]))
         ach_s = per_rank_flops / (kern_s * 1e-3) / 1e12
-        sustained = {"value": wl.flops * (1 if strong else world) / (ms_s * 1e-3) / 1e12, "ms_per_step": ms_s,
+        sustained = {"value": job_flops / (ms_s * 1e-3) / 1e12, "ms_per_step": ms_s,
                      "kernel_ms": kern_s, "achieved": ach_s, "peak": sus_peak, "frac": ach_s / sus_peak,
                      "peak_source": f"bf16_tflops_sustained of {peak_kind} peaks",
                      "what": "the same steps timed after %.1f s of identical steps (%d) without a pause"
@@ -652,7 +717,7 @@ def run_ours(args):
         run_w = Runner(wl, dev, 0, units_total, seed=wl.seed + 1000 * rank, kernel=args.kernel)
         for i in range(3):
             run_w.step(i)
-        ms_w, _ = time_steps(run_w.step, args.steps, stream, world)
+        ms_w = time_block(run_w.run_steps, args.steps, stream, world)
         weak = {"value": wl.flops * world / (ms_w * 1e-3) / 1e12, "ms_per_step": ms_w,
                 "what": "every rank runs the whole workload on its own inputs (replicas), no collective"}
         run_w.release()
@@ -718,7 +783,7 @@ def run_ours(args):
     h2d = sum(t.numel() * t.element_size() for t in hins if t is not None)
     d2h = hos[0].numel() * hos[0].element_size()
     barrier(world)
-    footprint, n_copies = run.footprint, len(run.sets)
+    footprint, n_copies, group = run.footprint, len(run.sets), run.group
     launches = run.launches_per_step()
     run.release()
     del run, q, k, v, o, dins, douts
@@ -749,11 +814,13 @@ def run_ours(args):
         "warmup": args.warmup, "ms_per_step": ms_step, "higher_is_better": True, "scaling": scaling,
         "vs_baseline": None, "dtype": DTYPE_NAMES[str(wl.dtype)],
         "data": "synthetic: seeded block mask; q, k, v ~ N(0,1) drawn on the device",
-        "config": config_dict(wl, world, scaling),
+        "config": dict(config_dict(wl, world, scaling), **({"units_timed": ranges[0][1]} if args.units else {})),
         "setup": {
             "units_per_rank": [b - a for a, b in ranges],
             "step": "attention forward with the plan built once per mask (the reference's timed loop reuses "
-                    "its block mask), replayed from a CUDA graph of the call" if not gather else
+                    "its block mask); the K steps are replayed from CUDA graphs of %d forwards back to back "
+                    "(then single-forward graphs for the remainder), exactly K forwards; the kernel time comes "
+                    "from events around single-forward replays" % group if not gather else
                     "attention forward per half of the rank's heads with the O gather to rank 0 posted after "
                     "each half (eager calls)",
             "l2": ("inputs larger than L2: %d input cop%s of q, k, v, o, %d MiB per rank, rotated per step"
@@ -765,10 +832,10 @@ def run_ours(args):
                      "peak_source": f"bf16_tflops (burst) of {peak_kind} peaks"},
         "plan_build_ms": t_plan,
         "with_plan_build": None if ms_plan_step is None else {
-            "value": wl.flops * (1 if strong else world) / (ms_plan_step * 1e-3) / 1e12,
+            "value": job_flops / (ms_plan_step * 1e-3) / 1e12,
             "ms_per_step": ms_plan_step, "what": "plan rebuilt from the mask every step (eager calls)"},
         "weak": weak,
-        "e2e": {"value": wl.flops * (1 if strong else world) / (e2e_ms * 1e-3) / 1e12, "unit": UNIT,
+        "e2e": {"value": job_flops / (e2e_ms * 1e-3) / 1e12, "unit": UNIT,
                 "ms_per_step": e2e_ms, "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
                 "path": "block_sparse_attention(q, k, v, mask) from pinned host buffers (plan built inside each "
                         "call); per step H2D of q, k, v, mask (+perms) and D2H of o, pipelined on copy streams"},
@@ -804,6 +871,8 @@ def main(argv=None):
     ap.add_argument("--kernel", default="auto", help="kernel choice passed to block_sparse_attention")
     ap.add_argument("--configs", default=",".join(CONFIGS), help="configurations of the per-config object")
     ap.add_argument("--ncu-csv", default=None, help="ncu raw CSV of the same command: roofline traffic from it")
+    ap.add_argument("--units", type=int, default=0,
+                    help="time only the first U (b,h) units of the workload (a smaller case for ncu captures)")
     args = ap.parse_args(argv)
     if args.warmup < 3:
         ap.error("--warmup must be >= 3")

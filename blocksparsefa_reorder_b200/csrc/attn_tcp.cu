@@ -15,12 +15,19 @@
 // through a small ring in shared memory.  The counter is one of kWorkSlots per device, taken in turn
 // by successive launches; the last CTA to finish resets it.  Roles:
 //  * warp 0, one thread: TMA producer (Q per tile, then K_g and V_g-1 per
-//    step, V one step behind K because PV_g-1 is issued after S_g; both land
-//    on one barrier, so the MMA issuer waits once per step for its data);
+//    step, V one step behind K because PV_g-1 is issued after S_g; each on
+//    its own barrier).  Before it blocks on a full tile ring it loads the V
+//    still pending, and the MMA issuer issues a pending PV before it blocks
+//    on a ring entry not yet written: the tile those end may be the one the
+//    ring waits for (runs of empty tiles fill the ring without any load);
 //  * warp 1, one thread: tcgen05.mma issuer (S_g = Q K_g^T, then PV_g-1);
-//  * warpgroup 1: softmax, one query row per thread, P written back into
-//    the first BS/2 columns of S's TMEM;
-//  * warpgroup 2: epilogue, one query row per thread: O / l from TMEM
+//  * warpgroups 1 and 2: softmax, two threads per query row (lanes i and
+//    i ^ 16 of a warp, half of the step's scores each; warpgroup 1 takes
+//    lanes 0-15 of every 32-lane TMEM quarter, warpgroup 2 lanes 16-31), P
+//    written back into the first BS/2 columns of S's TMEM.  Two softmax warps
+//    share each SM sub-partition, so one's waits and TMEM round trips overlap
+//    the other's exponentials;
+//  * warpgroup 3: epilogue, one query row per thread: O / l from TMEM
 //    straight to global memory, lse, and the zero rows of empty tiles;
 //  * warps 2-3, with a query permutation only: gather the tile's Q rows
 //    q[q_perm[row]] into the Q buffer (the layout the TMA load would give).
@@ -41,8 +48,9 @@
 //  * S_g+2 reuses S_g's TMEM and is issued after PV_g, which reads P_g there;
 //  * S_g complete implies PV_g-2 complete, and PV_g-1 completes before any
 //    later MMA: the softmax's rescale of O waits step_done of PV_g-1;
-//  * one commit per step (step_done[g % 4], after PV_g) frees K and V
-//    stages: it tracks S_g+1 (issued before PV_g) and PV_g;
+//  * S_g complete (s_full, seen by softmax warp 0, which then arrives on
+//    k_empty) frees K_g's stage; the commit after PV_g (step_done[g % 4])
+//    frees V_g's stage and lets a rescale of O go ahead;
 //  * Q_e's buffer is released (q_empty) by a commit after the tile's last S;
 //  * the first PV of tile e+2 waits o_empty[e&1]: the epilogue has read O_e.
 // Every wait is bounded by %globaltimer; a timeout sets BSA_DEVERR_TIMEOUT
@@ -70,11 +78,13 @@ std::atomic<unsigned> g_launches{0};
 std::atomic<uint32_t> g_test_wait_us{0};
 
 constexpr int kTileRing = 8;   // tile numbers in flight between the producer and the other roles
-// readers of each tile-ring entry: MMA thread + 4 softmax + 4 epilogue warps,
+// readers of each tile-ring entry: MMA thread + 8 softmax + 4 epilogue warps,
 // and the 2 Q-gather warps when there is a query permutation (without one they
 // leave at once rather than poll the ring next to the softmax warps)
-constexpr int kTileUsers = 9;
-constexpr int kTileUsersGather = 11;
+constexpr int kTileUsers = 13;
+constexpr int kTileUsersGather = 15;
+constexpr int kSoftmaxWarps = 8;
+
 
 // One claimed tile as the producer hands it to the other roles: the tile
 // number (-1 = no more), its plan entries e0 .. e0+n, its (b, h) and tile row.
@@ -115,14 +125,15 @@ struct TcpParams {
 constexpr int kPairMinEntries = 32;
 
 constexpr int kSmemLimitP = 232448;
-constexpr int kThreadsP = 384;
-// setmaxnreg split over the three warpgroups; the launch holds 168 per thread
-// (65536 / 384 rounded down to a multiple of 8).
-constexpr int kRegsLaunchP = 168;
-constexpr int kRegsIssueP = 72;
-constexpr int kRegsSoftmaxP = 240;
+constexpr int kThreadsP = 512;
+// setmaxnreg split over the four warpgroups (producer / MMA / Q gather, two
+// softmax, epilogue); the launch holds 128 per thread (65536 / 512).
+constexpr int kRegsLaunchP = 128;
+constexpr int kRegsIssueP = 64;
+constexpr int kRegsSoftmaxP = 176;
 constexpr int kRegsEpilogueP = 96;
-static_assert(128 * (kRegsIssueP + kRegsSoftmaxP + kRegsEpilogueP) <= kThreadsP * kRegsLaunchP, "register split");
+constexpr int kRegsSplitP = kRegsIssueP + 2 * kRegsSoftmaxP + kRegsEpilogueP;
+static_assert(128 * kRegsSplitP <= kThreadsP * kRegsLaunchP, "register split");
 
 __device__ __forceinline__ int64_t load_perm(const void* perm, int dtype, int64_t i) {
   return dtype == BSA_INDEX_I64 ? __ldg(static_cast<const int64_t*>(perm) + i)
@@ -145,21 +156,26 @@ struct TcpCfg {
   static constexpr int BOX_BYTES = BN * 128;  // one entry's rows of one 64-column chunk
   static constexpr int Q_BYTES = BM * D * 2;
   static constexpr int KV_BYTES = BS * D * 2;
-  static constexpr int BAR_BYTES = 768;
+  // barriers (2 KS + VS + 21 + 2 kTileRing), TMEM slot and abort flag, then the tile ring
+  static constexpr int ring_off(int ks, int vs) { return ((2 * ks + vs + 21 + 2 * kTileRing) * 8 + 8 + 15) / 16 * 16; }
+  static constexpr int bar_bytes(int ks, int vs) {
+    return (ring_off(ks, vs) + kTileRing * static_cast<int>(sizeof(TileSlot)) + 127) / 128 * 128;
+  }
   static constexpr int STATS_BYTES = 2 * 2 * BM * 4;  // [buffer][m, l][row] fp32
   static constexpr bool fits(int ks, int vs) {
-    return 2 * Q_BYTES + (ks + vs) * KV_BYTES + BAR_BYTES + STATS_BYTES <= kSmemLimitP;
+    return 2 * Q_BYTES + (ks + vs) * KV_BYTES + bar_bytes(ks, vs) + STATS_BYTES <= kSmemLimitP;
   }
   // K_j is released when S_j completes, V_j only when PV_j does: K gets the deeper ring.
   static constexpr int KS = fits(4, 4) || fits(4, 3) ? 4 : 3;
   static constexpr int VS = fits(4, 4) ? 4 : fits(4, 3) ? 3 : 2;
+  static constexpr int BAR_BYTES = bar_bytes(KS, VS);
   static constexpr int SMEM = 2 * Q_BYTES + (KS + VS) * KV_BYTES + BAR_BYTES + STATS_BYTES;
   static constexpr int O_COL0 = 2 * BS;
   static constexpr int TMEM_COLS = 2 * BS + 2 * D <= 256 ? 256 : 512;
   static_assert(SMEM <= kSmemLimitP, "shared memory budget");
   static_assert(2 * BS + 2 * D <= 512, "TMEM budget");
   static_assert(SUB * BN == BS && (SUB == 1 || SUB == 2) && (!PAIR || BN == 64), "block size");
-  static constexpr int RING_OFF = ((KS + 21 + 2 * kTileRing) * 8 + 8 + 15) / 16 * 16;
+  static constexpr int RING_OFF = ring_off(KS, VS);
   static_assert(RING_OFF + kTileRing * static_cast<int>(sizeof(TileSlot)) <= BAR_BYTES, "barrier area");
 };
 
@@ -181,16 +197,16 @@ __global__ void __launch_bounds__(kThreadsP, 1)
   float* stats = reinterpret_cast<float*>(reinterpret_cast<uint8_t*>(bars) + C::BAR_BYTES);
   uint64_t* q_full = bars;               // [2]
   uint64_t* q_empty = q_full + 2;        // [2] the tile's last S has read Q
-  // [KS] by step g % KS: K_g and V_g-1 (issued together) have landed
-  uint64_t* kv_full = q_empty + 2;
-  uint64_t* s_full = kv_full + KS;       // [2] by S buffer
-  uint64_t* p_ready = s_full + 2;        // [2] by S buffer, 4 softmax warps
+  uint64_t* k_full = q_empty + 2;        // [KS] by step g % KS: K_g landed
+  uint64_t* k_empty = k_full + KS;       // [KS] by step g % KS: S_g completed (K_g's stage free)
+  uint64_t* v_full = k_empty + KS;       // [VS] by step g % VS: V_g landed
+  uint64_t* s_full = v_full + VS;        // [2] by S buffer
+  uint64_t* p_ready = s_full + 2;        // [2] by S buffer, 8 softmax warps
   uint64_t* o_final = p_ready + 2;       // [2] by O buffer: the tile's last PV completed
   uint64_t* o_empty = o_final + 2;       // [2] by O buffer: 4 epilogue warps read O
-  uint64_t* stats_ready = o_empty + 2;   // [2] 4 softmax warps wrote (m, l)
+  uint64_t* stats_ready = o_empty + 2;   // [2] 8 softmax warps wrote (m, l)
   uint64_t* stats_empty = stats_ready + 2;  // [2] 4 epilogue warps read (m, l)
-  // [4] by step g % 4: one commit after PV_g tracks PV_g and every earlier MMA
-  // (S_g+1 among them): it frees K and V stages and lets a rescale of O go ahead
+  // [4] by step g % 4: the commit after PV_g (V_g's stage free, O up to PV_g complete)
   uint64_t* step_done = stats_empty + 2;
   uint64_t* drain = step_done + 4;
   uint64_t* tile_ready = drain + 1;              // [kTileRing] producer wrote the entry
@@ -208,13 +224,17 @@ __global__ void __launch_bounds__(kThreadsP, 1)
       mbar_init(&q_full[i], p.q_perm ? 2 : 1);  // gather warps, or the TMA transaction
       mbar_init(&q_empty[i], 1);
       mbar_init(&s_full[i], 1);
-      mbar_init(&p_ready[i], 4);
+      mbar_init(&p_ready[i], kSoftmaxWarps);
       mbar_init(&o_final[i], 1);
       mbar_init(&o_empty[i], 4);
-      mbar_init(&stats_ready[i], 4);
+      mbar_init(&stats_ready[i], kSoftmaxWarps);
       mbar_init(&stats_empty[i], 4);
     }
-    for (int i = 0; i < KS; ++i) mbar_init(&kv_full[i], 1);
+    for (int i = 0; i < KS; ++i) {
+      mbar_init(&k_full[i], 1);
+      mbar_init(&k_empty[i], 1);
+    }
+    for (int i = 0; i < VS; ++i) mbar_init(&v_full[i], 1);
     for (int i = 0; i < 4; ++i) mbar_init(&step_done[i], 1);
     mbar_init(drain, 1);
     for (int i = 0; i < kTileRing; ++i) {
@@ -289,27 +309,25 @@ __global__ void __launch_bounds__(kThreadsP, 1)
       int pv_b = 0, pv_h = 0;    // the step whose V is still to load (gv < g)
       int pv_kb[C::SUB] = {};
       bool ok = true;
-      int armed = 0;   // kv_full phases armed so far (one per step, one more for the last V)
       int qarmed = 0;  // Q tiles loaded by TMA so far
-      // the barrier of step gs's K may be re-armed once S_gs-KS completed: the commit
-      // after PV_gs-KS-1 (S_0 and S_1 both under the one after PV_0)
+      // step gs's K stage is free once S_gs-KS completed
       auto wait_k_stage = [&](int gs) -> bool {
-        const int sd = gs - KS - 1 > 0 ? gs - KS - 1 : 0;
-        return gs < KS || mbar_wait(&step_done[sd & 3], (sd >> 2) & 1, abort_flag, p.err, p.wait_ns);
+        return gs < KS || mbar_wait(&k_empty[gs % KS], ((gs / KS) - 1) & 1, abort_flag, p.err, p.wait_ns);
       };
-      // V_gv's stage is free once PV_gv-VS completed
-      auto wait_v_stage = [&]() -> bool {
-        return gv < VS || mbar_wait(&step_done[(gv - VS) & 3], ((gv - VS) >> 2) & 1, abort_flag, p.err, p.wait_ns);
-      };
-      // V_gv into its stage, counted on the barrier of the step it travels with (bar)
-      auto load_v = [&](uint64_t* bar) {
+      // V of step gv (one step behind K: PV_gv is issued after S_gv+1) into
+      // its stage, free once PV_gv-VS completed
+      auto load_v = [&]() -> bool {
+        if (gv >= VS && !mbar_wait(&step_done[(gv - VS) & 3], ((gv - VS) >> 2) & 1, abort_flag, p.err, p.wait_ns))
+          return false;
         const int st = gv % VS;
+        mbar_arrive_expect_tx(&v_full[st], C::KV_BYTES);
 #pragma unroll
         for (int u = 0; u < C::SUB; ++u)
           for (int c = 0; c < C::NCHUNK; ++c)
-            tma_load_4d(sV + st * C::KV_BYTES + c * C::KV_CHUNK + u * C::BOX_BYTES, &tmV, bar, c * 64,
+            tma_load_4d(sV + st * C::KV_BYTES + c * C::KV_CHUNK + u * C::BOX_BYTES, &tmV, &v_full[st], c * 64,
                         pv_kb[u] * BN, pv_h, pv_b);
         ++gv;
+        return true;
       };
       for (int i = 0; ok; ++i) {
         // claim the next tile and pass its number on
@@ -318,7 +336,13 @@ __global__ void __launch_bounds__(kThreadsP, 1)
         const int ri = i % kTileRing;
         int e0 = 0, n = 0, b = 0, h = 0, t = 0;
         if (w >= 0) tile_info(w, e0, n, b, h, t);
-        if (i >= kTileRing && !(ok = mbar_wait(&tile_free[ri], ((i / kTileRing) - 1) & 1, abort_flag, p.err, p.wait_ns))) break;
+        if (i >= kTileRing) {
+          const uint32_t par = ((i / kTileRing) - 1) & 1;
+          // a full ring: a role is still on an earlier tile, whose last PV may
+          // need the V not loaded yet
+          if (!mbar_try_wait(&tile_free[ri], par) && gv < g && !(ok = load_v())) break;
+          if (!(ok = mbar_wait(&tile_free[ri], par, abort_flag, p.err, p.wait_ns))) break;
+        }
         tile_ring[ri].w = w;
         tile_ring[ri].e0 = e0;
         tile_ring[ri].n = n;
@@ -352,43 +376,27 @@ __global__ void __launch_bounds__(kThreadsP, 1)
               kb[u] = 0;
             }
           }
-          // K_g and (from the second step on) V_g-1 complete one phase of
-          // kv_full[st]: each load's bytes are announced before it is issued
-          // and the phase's one arrival comes last, so a V stage that never
-          // frees (a role gave up) leaves a phase that completes with K alone
-          ++armed;
-          mbar_expect_tx(&kv_full[st], C::KV_BYTES);
+          mbar_arrive_expect_tx(&k_full[st], C::KV_BYTES);
 #pragma unroll
           for (int u = 0; u < C::SUB; ++u)
             for (int c = 0; c < C::NCHUNK; ++c)
-              tma_load_4d(sK + st * C::KV_BYTES + c * C::KV_CHUNK + u * C::BOX_BYTES, &tmK, &kv_full[st], c * 64,
+              tma_load_4d(sK + st * C::KV_BYTES + c * C::KV_CHUNK + u * C::BOX_BYTES, &tmK, &k_full[st], c * 64,
                           kb[u] * BN, h, b);
-          if (gv < g && (ok = wait_v_stage())) {
-            mbar_expect_tx(&kv_full[st], C::KV_BYTES);
-            load_v(&kv_full[st]);
-          }
-          mbar_arrive(&kv_full[st]);
-          if (!ok) break;
+          if (gv < g && !(ok = load_v())) break;
           pv_b = b;
           pv_h = h;
 #pragma unroll
           for (int u = 0; u < C::SUB; ++u) pv_kb[u] = kb[u];
         }
       }
-      if (ok && gv < g) {
-        // the last V alone, on the barrier of step g (no K)
-        if ((ok = wait_k_stage(g) && wait_v_stage())) {
-          ++armed;
-          mbar_arrive_expect_tx(&kv_full[g % KS], C::KV_BYTES);
-          load_v(&kv_full[g % KS]);
-        }
-      }
+      if (ok && gv < g) ok = load_v();  // the last step's V
       // Every load this thread issued lands before the CTA exits, also when a
       // role gave up and the loads were never consumed: the last phase armed on
-      // each K/V barrier and on each Q barrier (all earlier phases completed
-      // before their barrier was re-armed).
-      for (int j = armed > KS ? armed - KS : 0; j < armed; ++j)
-        mbar_wait(&kv_full[j % KS], (j / KS) & 1, nullptr, nullptr, p.wait_ns);
+      // each K, V and Q barrier (all earlier phases completed before their
+      // stage was loaded again).
+      for (int j = g > KS ? g - KS : 0; j < g; ++j) mbar_wait(&k_full[j % KS], (j / KS) & 1, nullptr, nullptr, p.wait_ns);
+      for (int j = gv > VS ? gv - VS : 0; j < gv; ++j)
+        mbar_wait(&v_full[j % VS], (j / VS) & 1, nullptr, nullptr, p.wait_ns);
       for (int j = qarmed > 2 ? qarmed - 2 : 0; j < qarmed; ++j)
         mbar_wait(&q_full[j & 1], (j >> 1) & 1, nullptr, nullptr, p.wait_ns);
     } else if (warp == 1 && lane == 0) {
@@ -405,15 +413,13 @@ __global__ void __launch_bounds__(kThreadsP, 1)
       bool pend_first = false, pend_last = false;
       bool ok = true;
       int pv_issued_tiles = 0;  // non-empty tiles whose first PV was issued (o_empty accounting)
-      auto do_pv = [&](bool last_pv) -> bool {
+      auto do_pv = [&]() -> bool {
         const int i = pend_j, st = i % VS;
         if (pend_first && pv_issued_tiles >= 2 &&
             !mbar_wait(&o_empty[pend_ob], ((pv_issued_tiles >> 1) - 1) & 1, abort_flag, p.err, p.wait_ns))
           return false;
         if (!mbar_wait(&p_ready[i & 1], (i >> 1) & 1, abort_flag, p.err, p.wait_ns)) return false;
-        // V_i landed with K_i+1 (kv_full of step i+1, waited before S_i+1 was issued), or
-        // alone after the last step
-        if (last_pv && !mbar_wait(&kv_full[(i + 1) % KS], ((i + 1) / KS) & 1, abort_flag, p.err, p.wait_ns)) return false;
+        if (!mbar_wait(&v_full[st], (i / VS) & 1, abort_flag, p.err, p.wait_ns)) return false;
         tc_fence_after();
         const uint32_t p_tmem = tmem + (i & 1) * C::BS;  // P_i lives in the first columns of S buffer i&1
         const uint32_t o_tmem = tmem + C::O_COL0 + pend_ob * D;
@@ -429,6 +435,9 @@ __global__ void __launch_bounds__(kThreadsP, 1)
         return true;
       };
       for (int i = 0; ok; ++i) {
+        // the next tile not announced yet: issue the pending PV now (the tile
+        // it ends may be what the ring waits for)
+        if (pend_j >= 0 && !mbar_try_wait(&tile_ready[i % kTileRing], (i / kTileRing) & 1) && !(ok = do_pv())) break;
         int w, e0, n, b, h, t;
         next_tile(i, w, e0, n, b, h, t);
         mbar_arrive(&tile_free[i % kTileRing]);
@@ -440,7 +449,7 @@ __global__ void __launch_bounds__(kThreadsP, 1)
         const int nsteps = (n + C::SUB - 1) / C::SUB;
         for (int j = 0; j < nsteps; ++j, ++jg) {
           const int st = jg % KS;
-          if (!(ok = mbar_wait(&kv_full[st], (jg / KS) & 1, abort_flag, p.err, p.wait_ns))) break;
+          if (!(ok = mbar_wait(&k_full[st], (jg / KS) & 1, abort_flag, p.err, p.wait_ns))) break;
           tc_fence_after();
           const uint32_t d_tmem = tmem + (jg & 1) * C::BS;
 #pragma unroll
@@ -452,7 +461,7 @@ __global__ void __launch_bounds__(kThreadsP, 1)
           }
           tc_commit(&s_full[jg & 1]);
           if (j == nsteps - 1) tc_commit(&q_empty[qb]);
-          if (pend_j >= 0 && !(ok = do_pv(false))) break;
+          if (pend_j >= 0 && !(ok = do_pv())) break;
           pend_j = jg;
           pend_ob = e & 1;
           pend_first = j == 0;
@@ -460,7 +469,7 @@ __global__ void __launch_bounds__(kThreadsP, 1)
         }
         ++e;
       }
-      if (ok && pend_j >= 0) ok = do_pv(true);
+      if (ok && pend_j >= 0) ok = do_pv();
       tc_commit(drain);
       mbar_wait(drain, 0, nullptr, nullptr, p.wait_ns);
     } else if (warp >= 2 && p.q_perm) {
@@ -508,13 +517,16 @@ __global__ void __launch_bounds__(kThreadsP, 1)
         if (lane == 0) mbar_arrive(&q_full[qb]);
       }
     }
-  } else if (warp < 8) {
+  } else if (warp < 12) {
     regs_inc<kRegsSoftmaxP>();
     // -------------------------------------------------------------- softmax
-    const int q4 = warp & 3;  // TMEM lane quarter this warp may access
-    const int row = q4 * 32 + lane;
-    const uint32_t lane_base = tmem + (static_cast<uint32_t>(q4 * 32) << 16);
+    const int hw = (warp - 4) >> 2;  // softmax warpgroup: lanes 0-15 or 16-31 of the quarter
+    const int q4 = warp & 3;         // TMEM lane quarter this warp may access
+    const int sub = lane >> 4;       // which half of the row's scores this thread holds
+    const int row = q4 * 32 + hw * 16 + (lane & 15);
+    const uint32_t lane_base = tmem + (static_cast<uint32_t>(q4 * 32 + hw * 16) << 16);
     const int half = row >> 6;
+    constexpr int HB = C::BS / 2;  // scores per thread per step
     int e = 0, jg = 0;
     bool ok = true;
     for (int i = 0;; ++i) {
@@ -533,13 +545,15 @@ __global__ void __launch_bounds__(kThreadsP, 1)
         if (!(ok = ok && __all_sync(0xffffffffu, mbar_wait(&s_full[sb], (jg >> 1) & 1, abort_flag, p.err, p.wait_ns))))
           continue;
         tc_fence_after();
-        uint32_t sr[C::BS];
-#pragma unroll
-        for (int c = 0; c < C::BS / 32; ++c) tmem_ld32(lane_base + sb * C::BS + c * 32, &sr[c * 32]);
+        // S_jg complete: the tensor cores are done with K_jg's stage
+        if (warp == 4 && lane == 0) mbar_arrive(&k_empty[jg % KS]);
+        uint32_t sr[HB];
+        tmem_ld16x2<HB, HB>(lane_base + sb * C::BS, sr);
         tmem_wait_ld();
         // Per plan entry of the step: whether this row's query block keeps it
         // (per-half flags at BN 64; a missing second entry is never kept) and
-        // how many of its keys lie before N (TMA zero-filled the rest).
+        // how many of its keys lie before N (TMA zero-filled the rest).  The
+        // same for all rows of a warp (they share a 64-row query block).
         bool act[C::SUB];
         int kvalid[C::SUB];
         bool any = false, need_mask = false;
@@ -552,16 +566,19 @@ __global__ void __launch_bounds__(kThreadsP, 1)
           any = any || act[u];
           need_mask = need_mask || !act[u] || kvalid[u] < BN;
         }
-        uint32_t pr[C::BS / 2];
+        uint32_t pr[HB / 2];
         if (any) {
-          if (need_mask) {  // (uniform per warp: a warp's 32 rows share a query block)
+          if (need_mask) {
+            // this thread's HB keys lie in one entry of the step (HB divides BN)
+            const int u = sub * HB / BN;
+            const bool act_u = C::SUB == 1 || u == 0 ? act[0] : act[C::SUB - 1];
+            const int kvalid_u = C::SUB == 1 || u == 0 ? kvalid[0] : kvalid[C::SUB - 1];
+            const int key0 = sub * HB - u * BN;  // key of sr[0] within that entry
 #pragma unroll
-            for (int i = 0; i < C::BS; ++i) {
-              const int u = i / BN;
-              if (!act[u] || i - u * BN >= kvalid[u]) sr[i] = __float_as_uint(-INFINITY);
-            }
+            for (int i = 0; i < HB; ++i)
+              if (!act_u || key0 + i >= kvalid_u) sr[i] = __float_as_uint(-INFINITY);
           }
-          const float alpha = softmax_block<C::BS, BF16>(sr, pr, p.scale_log2, m_run, l_run);
+          const float alpha = softmax_block_split<HB, BF16>(sr, pr, p.scale_log2, m_run, l_run);
           if (__any_sync(0xffffffffu, alpha != 1.f)) {
             // O holds the sum up to block j-1 of this tile: wait for that PV, rescale in TMEM.
             if (!(ok = __all_sync(0xffffffffu,
@@ -569,32 +586,34 @@ __global__ void __launch_bounds__(kThreadsP, 1)
               continue;
             tc_fence_after();
 #pragma unroll
-            for (int c = 0; c < D / 32; ++c) {
+            for (int c = 0; c < D / 64; ++c) {
               uint32_t o[32];
-              tmem_ld32(lane_base + C::O_COL0 + ob * D + c * 32, o);
+              tmem_ld16x2<32, D / 2>(lane_base + C::O_COL0 + ob * D + c * 32, o);
               tmem_wait_ld();
 #pragma unroll
               for (int i = 0; i < 32; ++i) o[i] = __float_as_uint(__uint_as_float(o[i]) * alpha);
-              tmem_st32(lane_base + C::O_COL0 + ob * D + c * 32, o);
+              tmem_st16x2<32, D / 2>(lane_base + C::O_COL0 + ob * D + c * 32, o);
             }
           }
         } else {
 #pragma unroll
-          for (int i = 0; i < C::BS / 2; ++i) pr[i] = 0u;
+          for (int i = 0; i < HB / 2; ++i) pr[i] = 0u;
         }
         // P_j into the first BS/2 columns of its S buffer (all of S is in registers)
-#pragma unroll
-        for (int c = 0; c < C::BS / 64; ++c) tmem_st32(lane_base + sb * C::BS + c * 32, &pr[c * 32]);
+        tmem_st16x2<HB / 2, HB / 2>(lane_base + sb * C::BS, pr);
         tmem_wait_st();
         tc_fence_before();
         __syncwarp();
-        if (lane == 0 && !(p.withhold_arrive && jg == 0 && q4 == 0 && blockIdx.x == 0)) mbar_arrive(&p_ready[sb]);
+        if (lane == 0 && !(p.withhold_arrive && jg == 0 && q4 == 0 && hw == 0 && blockIdx.x == 0))
+          mbar_arrive(&p_ready[sb]);
       }
       // hand the row's (m, l) to the epilogue warps
       if (e >= 2)
         ok = ok && __all_sync(0xffffffffu, mbar_wait(&stats_empty[ob], ((e >> 1) - 1) & 1, abort_flag, p.err, p.wait_ns));
-      stats[ob * 256 + row] = m_run;
-      stats[ob * 256 + 128 + row] = l_run;
+      if (sub == 0) {
+        stats[ob * 256 + row] = m_run;
+        stats[ob * 256 + 128 + row] = l_run;
+      }
       __syncwarp();
       if (lane == 0) mbar_arrive(&stats_ready[ob]);
       ++e;
@@ -770,7 +789,7 @@ int launch_p(const bsa_fwd_args* a, cudaStream_t st, const void* q_perm, int per
   if (!checked.load(std::memory_order_relaxed)) {
     cudaFuncAttributes fa;
     BSA_CUDA_CHECK(cudaFuncGetAttributes(&fa, kern));
-    checked.store(fa.numRegs * kThreadsP >= 128 * (kRegsIssueP + kRegsSoftmaxP + kRegsEpilogueP) ? 1 : 2);
+    checked.store(fa.numRegs * kThreadsP >= 128 * kRegsSplitP ? 1 : 2);
   }
   if (checked.load(std::memory_order_relaxed) != 1) return BSA_ERR_UNSUPPORTED;
   // the shared-memory opt-in, once per device

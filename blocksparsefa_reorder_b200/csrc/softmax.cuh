@@ -109,4 +109,36 @@ __device__ __forceinline__ float softmax_block(const uint32_t (&sr)[BN], uint32_
   return alpha;
 }
 
+// The same for a row whose scores are split between two threads of a warp
+// (lanes i and i ^ 16, BN scores each): the row max and the block sum are
+// combined with one shuffle, so both threads take the same decisions and keep
+// the same m_run / l_run.  Every thread of the warp calls it: the first-block
+// max and the redo run warp-wide when any row of the warp needs them (a row
+// redone without need gets the same reference point or a larger one, and
+// alpha rescales its O and l either way).
+template <int BN, bool BF16>
+__device__ __forceinline__ float softmax_block_split(const uint32_t (&sr)[BN], uint32_t (&pr)[BN / 2],
+                                                     float scale_log2, float& m_run, float& l_run) {
+  if (__any_sync(0xffffffffu, m_run == -INFINITY)) {
+    float mx = row_max<BN>(sr);
+    mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 16));
+    if (m_run == -INFINITY) m_run = mx * scale_log2;
+  }
+  float ls = exp_block<BN, BF16>(sr, pr, scale_log2, -m_run);
+  ls += __shfl_xor_sync(0xffffffffu, ls, 16);
+  float alpha = 1.f;
+  if (__any_sync(0xffffffffu, !(ls <= ref_slack<BF16>()))) {
+    float mx = row_max<BN>(sr);
+    mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 16));
+    const float m_new = fmaxf(m_run, mx * scale_log2);
+    alpha = ex2_approx(m_run - m_new);
+    l_run *= alpha;
+    m_run = m_new;
+    ls = exp_block<BN, BF16>(sr, pr, scale_log2, -m_run);
+    ls += __shfl_xor_sync(0xffffffffu, ls, 16);
+  }
+  l_run += ls;
+  return alpha;
+}
+
 }  // namespace bsa

@@ -333,6 +333,37 @@ def _torch_masked_reference(q, k, v, mask, block, sm_scale):
     return o, lse
 
 
+@pytest.mark.parametrize("block", [64, 128])
+def test_runs_of_empty_tiles(dev, block):
+    """Each head keeps key blocks only in its first 128-row tile (many key
+    blocks, so that tile has many steps) and every other tile of the head is
+    empty, so a CTA claims one long tile and then runs of empty tiles, which
+    fill the producer's tile ring without any load: the tile's last V and
+    last PV must still be issued while the ring is full (the roles that free
+    the ring wait for that tile's output).  No timeout, and O / lse against
+    the fp32 reference on sampled heads (the empty rows: O = 0, lse = -inf)."""
+    B, H, D = 1, 160, 64
+    N = 40 * 128 - 32  # 40 tiles per head, a partial last key block
+    nb = (N + block - 1) // block
+    mask = np.zeros((1, H, nb, nb), dtype=bool)
+    rows = 128 // block
+    rng = np.random.default_rng(23)
+    mask[0, :, :rows, :] = rng.random((H, rows, nb)) < 0.5
+    mask[0, :, :rows, 0] = True
+    q, k, v = _qkv(B, H, N, D, torch.bfloat16, seed=24, dev=dev)
+    plan = BlockSparsePlan(torch.from_numpy(mask).to(dev), block)
+    for _ in range(3):
+        o, lse = block_sparse_attention(q, k, v, plan=plan, kernel="tcgen05", return_lse=True, check_errors=True)
+    heads = [0, 77, H - 1]
+    ref_o, ref_lse = _torch_masked_reference(q[:, heads], k[:, heads], v[:, heads], mask[:, heads], block,
+                                             1.0 / math.sqrt(D))
+    assert (o[:, heads].float() - ref_o).abs().max().item() <= TOL_16
+    fin = torch.isfinite(ref_lse)
+    assert torch.equal(torch.isfinite(lse[:, heads]), fin)
+    assert (lse[:, heads][fin] - ref_lse[fin]).abs().max().item() <= TOL_LSE
+    assert torch.count_nonzero(o[:, :, 128:]) == 0
+
+
 @pytest.mark.parametrize("D,block", [(64, 64), (128, 64), (64, 128), (128, 128)])
 def test_many_tiles_per_cta(dev, D, block):
     """Several times more 128-row tiles than SMs, so each CTA of the
