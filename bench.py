@@ -64,8 +64,13 @@ CONFIGS = ["plumbing", "random", "sbm", "headline", "longctx", "sweep_p01", "swe
 # same workload (dram__bytes_read.sum + dram__bytes_write.sum), with the
 # command that produced it; --ncu-csv takes the figure from a capture instead.
 NCU_TRAFFIC = {
-    "headline": (249916160.0, "ncu --set full --clock-control none -k regex:attn_tcp -s 3 -c 1 "
-                              "python bench.py --steps 10 --warmup 3 --no-cpu-baseline (headline workload)"),
+    "headline": (249925376.0, "ncu --set full --clock-control none -k regex:attn_tcp -s 3 -c 1 python bench.py "
+                              "--steps 10 --warmup 3 --no-cpu-baseline --no-per-config --sustained-seconds 0 "
+                              "(headline workload)"),
+    "sweep_p20": (4043484160.0, "ncu --set full --clock-control none -k regex:attn_tcp -s 24 -c 2 python bench.py "
+                                "--workload sweep_p20 --units 8 --steps 5 --warmup 3 --no-cpu-baseline "
+                                "--no-per-config --sustained-seconds 0, DRAM bytes of the 8-unit launch x 16 "
+                                "(the 128 units are independent)"),
 }
 
 
@@ -590,6 +595,8 @@ def measure_config(name, dev, peaks, steps=10, warmup=3, kernel="auto"):
                                          % (qbs, units - 1),
         "clocks": clocks,
     }
+    if name in NCU_TRAFFIC:
+        out["traffic"], out["traffic_source"] = NCU_TRAFFIC[name][0], "committed ncu capture: " + NCU_TRAFFIC[name][1]
     run.release()
     del run
     torch.cuda.empty_cache()
