@@ -7,6 +7,10 @@ block_sparse_attention(q, k, v, block_mask, *, q_perm=None, kv_perm=None, ...)
     permutations) in, output in original token order out.
 BlockSparsePlan(block_mask, block)
     the per-tile list of kept key blocks, built on the GPU, reusable.
+block_sparse_attention_backward(q, k, v, o, lse, dout, *, plan, plan_t, ...)
+    gradients dq, dk, dv (BLOCK 128, bf16 / fp16, D 64 / 128; beyond the
+    reference, which has no backward); block_sparse_attention_autograd wraps
+    forward and backward as a differentiable op.
 kernels.attn_fwd_block_sparse / attn_fwd_block_sparse_perm
     drop-ins for the reference's two Triton launches.
 utils
@@ -23,8 +27,10 @@ The CUDA kernels live in ``_lib/libbsattn_b200.so`` (built by
 """
 
 from ._lib import BsaError
-from .api import BlockSparsePlan, block_sparse_attention, infer_block, inverse_permutation, permute_rows
+from .api import (BlockSparsePlan, block_sparse_attention, block_sparse_attention_autograd,
+                  block_sparse_attention_backward, infer_block, inverse_permutation, permute_rows, transposed_plan)
 
-__all__ = ["BsaError", "BlockSparsePlan", "block_sparse_attention", "infer_block", "inverse_permutation",
-           "permute_rows"]
+__all__ = ["BsaError", "BlockSparsePlan", "block_sparse_attention", "block_sparse_attention_autograd",
+           "block_sparse_attention_backward", "infer_block", "inverse_permutation", "permute_rows",
+           "transposed_plan"]
 __version__ = "0.1.0"

@@ -45,6 +45,14 @@ class FwdArgs(ctypes.Structure):
                 ("err_flag", ctypes.c_void_p), ("kernel", ctypes.c_int32)]
 
 
+class BwdArgs(ctypes.Structure):
+    _fields_ = [("B", ctypes.c_int32), ("H", ctypes.c_int32), ("N", ctypes.c_int32), ("D", ctypes.c_int32),
+                ("dtype", ctypes.c_int32), ("q", Tensor4d), ("k", Tensor4d), ("v", Tensor4d), ("o", Tensor4d),
+                ("dout", Tensor4d), ("dq", Tensor4d), ("dk", Tensor4d), ("dv", Tensor4d),
+                ("sm_scale", ctypes.c_float), ("lse", ctypes.c_void_p), ("delta", ctypes.c_void_p),
+                ("plan", Plan), ("plan_t", Plan), ("err_flag", ctypes.c_void_p)]
+
+
 class BsaError(RuntimeError):
     """A C-ABI call returned a non-zero bsa_status."""
 
@@ -72,6 +80,7 @@ PROTOS = {
     "bsa_fwd_reordered_workspace_bytes": ([ctypes.POINTER(FwdArgs), ctypes.POINTER(_sz)], ctypes.c_int),
     "bsa_fwd_reordered": ([ctypes.POINTER(FwdArgs), _vp, _vp, _i32, _vp, _sz, _vp], ctypes.c_int),
     "bsa_test_arm_wait_timeout": ([ctypes.c_uint32], ctypes.c_int),
+    "bsa_bwd": ([ctypes.POINTER(BwdArgs), _vp], ctypes.c_int),
 }
 EXPORTED = tuple(PROTOS)
 

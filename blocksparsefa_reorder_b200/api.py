@@ -264,6 +264,89 @@ def block_sparse_attention(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor,
     return (o, lse) if return_lse else o
 
 
+def transposed_plan(plan: BlockSparsePlan, block_mask: torch.Tensor) -> BlockSparsePlan:
+    """The plan of ``block_mask`` with its last two dims swapped: per key
+    block, the query blocks that keep it (what the backward's dK / dV kernel
+    walks)."""
+    m = BlockSparsePlan._as_mask(block_mask)
+    if (int(m.shape[0]), int(m.shape[1]), int(m.shape[2])) != (plan.mask_b, plan.mask_h, plan.nb):
+        raise ValueError("block_mask does not match the plan")
+    return BlockSparsePlan(m.transpose(-1, -2).contiguous(), plan.block)
+
+
+def block_sparse_attention_backward(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, o: torch.Tensor,
+                                    lse: torch.Tensor, dout: torch.Tensor, *, plan: BlockSparsePlan,
+                                    plan_t: BlockSparsePlan, sm_scale: Optional[float] = None,
+                                    check_errors: bool = False):
+    """Gradients of :func:`block_sparse_attention` (no token permutation):
+    returns ``dq, dk, dv`` for the output gradient ``dout``.
+
+    ``o`` and ``lse`` are the forward's output and log2 LSE
+    (``return_lse=True``); ``plan`` is the forward's plan and ``plan_t`` the
+    plan of the transposed block mask (:func:`transposed_plan`).  bf16 /
+    fp16, D 64 or 128, BLOCK 128, on the tcgen05 kernels; P is recomputed
+    from ``lse`` and every gradient row is written by one CTA (no atomics,
+    deterministic).  The reference has no backward pass.
+    """
+    for name, t in (("q", q), ("k", k), ("v", v), ("o", o), ("dout", dout), ("lse", lse)):
+        _require_cuda(t, name)
+    if q.dim() != 4 or any(t.shape != q.shape for t in (k, v, o, dout)):
+        raise ValueError("q, k, v, o, dout must share one [B, H, N, D] shape")
+    if q.dtype not in (torch.float16, torch.bfloat16) or any(t.dtype != q.dtype for t in (k, v, o, dout)):
+        raise TypeError("the backward takes float16 or bfloat16 q, k, v, o, dout of one dtype")
+    B, H, N, D = (int(x) for x in q.shape)
+    if tuple(lse.shape) != (B, H, N) or lse.dtype != torch.float32 or not lse.is_contiguous():
+        raise ValueError("lse must be the forward's contiguous float32 [B, H, N] LSE")
+    for pl in (plan, plan_t):
+        if pl.device != q.device:
+            raise ValueError("plan is on another device")
+    scale = 1.0 / math.sqrt(D) if sm_scale is None else float(sm_scale)
+    dq, dk, dv = (torch.empty_like(q) for _ in range(3))
+    delta = torch.empty((B, H, N), dtype=torch.float32, device=q.device)
+    err = torch.zeros(1, dtype=torch.int32, device=q.device) if check_errors else None
+    args = _lib.BwdArgs()
+    args.B, args.H, args.N, args.D = B, H, N, D
+    args.dtype = _DTYPES[q.dtype]
+    args.q, args.k, args.v, args.o, args.dout = _t4(q), _t4(k), _t4(v), _t4(o), _t4(dout)
+    args.dq, args.dk, args.dv = _t4(dq), _t4(dk), _t4(dv)
+    args.sm_scale = scale
+    args.lse = lse.data_ptr()
+    args.delta = delta.data_ptr()
+    args.plan = plan.c_plan()
+    args.plan_t = plan_t.c_plan()
+    args.err_flag = err.data_ptr() if err is not None else None
+    _lib.check(_lib.lib().bsa_bwd(ctypes.byref(args), _stream(q.device)), "bsa_bwd")
+    _check_err(err, "block_sparse_attention_backward")
+    return dq, dk, dv
+
+
+class _BlockSparseAttentionFn(torch.autograd.Function):
+    @staticmethod
+    def forward(ctx, q, k, v, plan, plan_t, sm_scale):
+        o, lse = block_sparse_attention(q, k, v, plan=plan, sm_scale=sm_scale, return_lse=True, kernel="tcgen05")
+        ctx.save_for_backward(q, k, v, o, lse)
+        ctx.plan, ctx.plan_t, ctx.sm_scale = plan, plan_t, sm_scale
+        return o
+
+    @staticmethod
+    def backward(ctx, dout):
+        q, k, v, o, lse = ctx.saved_tensors
+        dq, dk, dv = block_sparse_attention_backward(q, k, v, o, lse, dout.contiguous(), plan=ctx.plan,
+                                                     plan_t=ctx.plan_t, sm_scale=ctx.sm_scale)
+        return dq, dk, dv, None, None, None
+
+
+def block_sparse_attention_autograd(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor,
+                                    block_mask: torch.Tensor, *, block: int = 128,
+                                    sm_scale: Optional[float] = None) -> torch.Tensor:
+    """The forward as a differentiable op: ``o.backward(g)`` runs
+    :func:`block_sparse_attention_backward` (same restrictions)."""
+    plan = BlockSparsePlan(block_mask, block)
+    plan_t = transposed_plan(plan, block_mask)
+    scale = 1.0 / math.sqrt(int(q.shape[-1])) if sm_scale is None else float(sm_scale)
+    return _BlockSparseAttentionFn.apply(q, k, v, plan, plan_t, scale)
+
+
 def permute_rows(x: torch.Tensor, perm, dim: int, inverse: bool, out: Optional[torch.Tensor] = None,
                  check_errors: bool = False) -> torch.Tensor:
     """Gather (``inverse=False``: ``out.select(dim, i) = x.select(dim, perm[i])``)

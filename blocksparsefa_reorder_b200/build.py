@@ -24,7 +24,8 @@ INCLUDE = PKG.parent / "include"
 BUILD_DIR = PKG / "_build"
 LIB_DIR = PKG / "_lib"
 LIB_PATH = LIB_DIR / "libbsattn_b200.so"
-SOURCES = ["api.cu", "preprocess.cu", "attn_simt.cu", "tma_maps.cu", "attn_tcp.cu", "plan_noalloc.cu"]
+SOURCES = ["api.cu", "preprocess.cu", "attn_simt.cu", "tma_maps.cu", "attn_tcp.cu", "attn_bwd.cu",
+           "plan_noalloc.cu"]
 ARCH_FLAGS = ["-gencode", "arch=compute_100a,code=sm_100a"]
 CFLAGS = ["-O3", "-lineinfo", "-std=c++17", "-Xcompiler", "-fPIC", "-Xcompiler", "-fvisibility=hidden",
           "--expt-relaxed-constexpr"]

@@ -158,6 +158,33 @@ extern "C" int bsa_fwd(const bsa_fwd_args* a, void* stream) {
   }
 }
 
+extern "C" int bsa_bwd(const bsa_bwd_args* a, void* stream) {
+  if (!a) return BSA_ERR_INVALID_ARG;
+  if (a->B <= 0 || a->H <= 0 || a->N <= 0 || a->D <= 0) return BSA_ERR_INVALID_ARG;
+  if (a->dtype != BSA_DTYPE_F16 && a->dtype != BSA_DTYPE_BF16) return BSA_ERR_DTYPE;
+  const bsa_tensor4d* ts[] = {&a->q, &a->k, &a->v, &a->o, &a->dout, &a->dq, &a->dk, &a->dv};
+  for (const bsa_tensor4d* t : ts)
+    if (!valid_tensor(*t)) return BSA_ERR_INVALID_ARG;
+  if (!a->lse || !a->delta) return BSA_ERR_INVALID_ARG;
+  if (a->D != 64 && a->D != 128) return BSA_ERR_UNSUPPORTED;
+  const bsa_plan* ps[] = {&a->plan, &a->plan_t};
+  for (const bsa_plan* p : ps) {
+    if (!p->tile_ptr || !p->tile_col) return BSA_ERR_INVALID_ARG;
+    if (p->block != 128) return BSA_ERR_UNSUPPORTED;
+    if (p->nb != (a->N + 127) / 128) return BSA_ERR_SHAPE;
+    if (!(p->mask_b == 1 || p->mask_b == a->B) || !(p->mask_h == 1 || p->mask_h == a->H)) return BSA_ERR_SHAPE;
+  }
+  if (!(a->sm_scale > 0.f) || !isfinite(a->sm_scale)) return BSA_ERR_UNSUPPORTED;
+  for (const bsa_tensor4d* t : ts)
+    if ((reinterpret_cast<uintptr_t>(t->data) % 16) || (t->stride_n * 2) % 16 || (t->stride_h * 2) % 16 ||
+        (t->stride_b * 2) % 16)
+      return BSA_ERR_ALIGNMENT;
+  if (reinterpret_cast<uintptr_t>(a->delta) % 16) return BSA_ERR_ALIGNMENT;
+  int rc = check_device();
+  if (rc) return rc;
+  return launch_attn_bwd(a, static_cast<cudaStream_t>(stream));
+}
+
 extern "C" int bsa_fwd_reordered_workspace_bytes(const bsa_fwd_args* a, size_t* bytes) {
   if (!a || !bytes) return BSA_ERR_INVALID_ARG;
   const int rc = validate_fwd(a);

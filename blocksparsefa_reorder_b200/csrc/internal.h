@@ -32,6 +32,8 @@ int launch_permute_rows(bsa_tensor4d dst, bsa_tensor4d src, int B, int H, int N,
 
 // attn_simt.cu
 int launch_attn_simt(const bsa_fwd_args* a, cudaStream_t st);
+// The backward kernels (attn_bwd.cu): Delta, dQ, dK / dV; arguments validated.
+int launch_attn_bwd(const bsa_bwd_args* a, cudaStream_t st);
 
 // tma_maps.cu: whether the tcgen05 path takes these arguments (bf16 / fp16,
 // D 64 or 128, BLOCK 64 or 128, 16-byte-aligned rows), and the 4-D TMA map

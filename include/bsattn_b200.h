@@ -209,6 +209,33 @@ BSA_API int bsa_fwd_reordered_workspace_bytes(const bsa_fwd_args* args, size_t* 
 BSA_API int bsa_fwd_reordered(const bsa_fwd_args* args, const void* q_perm, const void* kv_perm,
                               int32_t perm_dtype, void* workspace, size_t workspace_bytes, void* stream);
 
+/* Backward pass (gradients of bsa_fwd), beyond the reference, whose kernels
+ * write the row LSE M (triton_kernels/BlockSparse_Naive.py:119-122) but have
+ * no backward.  tcgen05 path only: bf16 / fp16, D 64 or 128, BLOCK 128, no
+ * token permutation, 16-byte aligned rows.  From dout and the forward's o
+ * and lse it writes dq = sm_scale dS K, dk = sm_scale dS^T Q, dv = P^T dout
+ * (P recomputed from lse, dS = P o (dout V^T - rowsum(dout o o))), each
+ * output row by one CTA (deterministic, no atomics).
+ *  - lse: the forward's [B,H,N] fp32 LSE (log2 units), contiguous;
+ *  - delta: workspace, contiguous [B,H,N] fp32 (rowsum(dout o o) is written
+ *    there first);
+ *  - plan: the forward's plan (query tiles); plan_t: the plan of the
+ *    transposed block mask, mask[..., j, i] (key tiles), same BLOCK.
+ * Enqueues three kernels on `stream`. */
+typedef struct bsa_bwd_args {
+  int32_t B, H, N, D;
+  int32_t dtype;            /* bsa_dtype of every tensor below (f16 or bf16)      */
+  bsa_tensor4d q, k, v, o, dout;
+  bsa_tensor4d dq, dk, dv;  /* outputs                                            */
+  float sm_scale;           /* the forward's softmax scale                        */
+  const float* lse;
+  float* delta;
+  bsa_plan plan;
+  bsa_plan plan_t;
+  int32_t* err_flag;        /* optional device int32 for BSA_DEVERR_* bits        */
+} bsa_bwd_args;
+BSA_API int bsa_bwd(const bsa_bwd_args* args, void* stream);
+
 /* Test hook for the bounded device waits, not for production use.  Arms the
  * NEXT tcgen05 forward (bsa_fwd / bsa_fwd_reordered) of the process: every
  * mbarrier wait of its launch gives up after `wait_us` microseconds (100 ..

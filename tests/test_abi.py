@@ -103,3 +103,31 @@ def test_other_entry_points_validate_on_host():
     assert L.bsa_fwd_reordered(ctypes.byref(a), None, 0x1000, 1, None, 0, None) == 9   # workspace missing
     assert L.bsa_fwd_reordered(ctypes.byref(_args(kernel=1)), 0x1000, None, 1, None, 0, None) == 9
     assert L.bsa_fwd_reordered(ctypes.byref(a), 0x1000, None, 7, 0x1000, 1 << 30, None) == 3  # perm dtype
+
+
+def _bwd_args(**kw):
+    a = _lib.BwdArgs()
+    a.B, a.H, a.N, a.D = kw.get("B", 1), kw.get("H", 2), kw.get("N", 256), kw.get("D", 64)
+    a.dtype = kw.get("dtype", _lib.DTYPE_BF16)
+    fake = 0x1000
+    for t in ("q", "k", "v", "o", "dout", "dq", "dk", "dv"):
+        setattr(a, t, _lib.Tensor4d(fake, 2 * 256 * 64, 256 * 64, 64))
+    a.sm_scale = kw.get("scale", 0.125)
+    a.lse = kw.get("lse", fake)
+    a.delta = kw.get("delta", fake)
+    for pl in ("plan", "plan_t"):
+        setattr(a, pl, _lib.Plan(fake, fake, 1, 1, kw.get("nb", 2), kw.get("block", 128)))
+    return a
+
+
+def test_bwd_rejects_invalid_arguments_on_the_host():
+    L = _lib.lib()
+    assert L.bsa_bwd(None, None) == 1
+    assert L.bsa_bwd(ctypes.byref(_bwd_args(dtype=_lib.DTYPE_F32)), None) == 3   # f16 / bf16 only
+    assert L.bsa_bwd(ctypes.byref(_bwd_args(D=96)), None) == 5                   # D 64 / 128 only
+    assert L.bsa_bwd(ctypes.byref(_bwd_args(block=64, nb=4)), None) == 5         # BLOCK 128 only
+    assert L.bsa_bwd(ctypes.byref(_bwd_args(nb=3)), None) == 2                   # nb vs N
+    assert L.bsa_bwd(ctypes.byref(_bwd_args(lse=None)), None) == 1               # lse required
+    assert L.bsa_bwd(ctypes.byref(_bwd_args(delta=None)), None) == 1             # delta workspace required
+    assert L.bsa_bwd(ctypes.byref(_bwd_args(scale=-1.0)), None) == 5
+    assert L.bsa_bwd(ctypes.byref(_bwd_args(delta=0x1004)), None) == 4           # delta not 16-byte aligned
