@@ -603,6 +603,40 @@ def measure_config(name, dev, peaks, steps=10, warmup=3, kernel="auto"):
     return out
 
 
+def measure_backward(wl, dev, steps):
+    """The backward pass on the workload (BLOCK 128, no permutation): device
+    time of one block_sparse_attention_backward call (Delta, dQ, dK / dV
+    kernels) with the forward's o / lse and both plans resident, against the
+    usual 2.5x-forward flop count (5 GEMMs of the kept blocks)."""
+    import torch
+
+    from blocksparsefa_reorder_b200 import (BlockSparsePlan, block_sparse_attention,
+                                            block_sparse_attention_backward, transposed_plan)
+
+    if wl.block != 128 or wl.q_perm is not None or str(wl.dtype) == "torch.float32":
+        return None
+    q, k, v = wl.make_qkv(dev)
+    g = torch.Generator(device="cpu").manual_seed(wl.seed + 7)
+    dout = torch.randn(q.shape, generator=g).to(q.dtype).to(dev)
+    m = wl.mask_tensor(dev)
+    plan = BlockSparsePlan(m, wl.block)
+    plan_t = transposed_plan(plan, m)
+    o, lse = block_sparse_attention(q, k, v, plan=plan, return_lse=True, kernel="tcgen05")
+    for _ in range(3):
+        block_sparse_attention_backward(q, k, v, o, lse, dout, plan=plan, plan_t=plan_t)
+    stream = torch.cuda.current_stream(dev)
+    _, evs = time_steps(lambda i: block_sparse_attention_backward(q, k, v, o, lse, dout, plan=plan, plan_t=plan_t),
+                        max(3, min(steps, 20)), stream, 1, per_step_events=True)
+    ms = statistics.median(evs)
+    peaks, _ = load_peaks()
+    tf = 2.5 * wl.flops / (ms * 1e-3) / 1e12
+    return {"ms": ms, "tflops": tf, "frac": tf / float(peaks.get("bf16_tflops", FALLBACK_PEAKS["bf16_tflops"])),
+            "flops_counted": 2.5 * wl.flops,
+            "what": "dq, dk, dv of the workload from dout (bf16): Delta, dQ and dK/dV kernels, P recomputed from the "
+                    "forward's lse; flops counted as 2.5 x the forward's (the kernels recompute S and dP in both "
+                    "gradient kernels, 3.5 x)"}
+
+
 # ----------------------------------------------------------------------------- our arm
 def run_ours(args):
     import torch
@@ -800,6 +834,8 @@ def run_ours(args):
     if rank != 0:
         return 0
 
+    backward = measure_backward(wl, dev, args.steps) if world == 1 and not args.no_backward else None
+
     per_config = None
     if world == 1 and not args.no_per_config:
         per_config = {}
@@ -850,6 +886,8 @@ def run_ours(args):
         "clocks": clocks,
         "sustained": sustained,
     }
+    if backward is not None:
+        line["backward"] = backward
     if per_config is not None:
         line["per_config"] = per_config
     if not args.no_cpu_baseline and world == 1:
@@ -875,6 +913,7 @@ def main(argv=None):
     ap.add_argument("--ref-budget-s", type=float, default=90.0, help="total CPU time of the reference arm")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-per-config", action="store_true")
+    ap.add_argument("--no-backward", action="store_true", help="skip the backward-pass measurement")
     ap.add_argument("--kernel", default="auto", help="kernel choice passed to block_sparse_attention")
     ap.add_argument("--configs", default=",".join(CONFIGS), help="configurations of the per-config object")
     ap.add_argument("--ncu-csv", default=None, help="ncu raw CSV of the same command: roofline traffic from it")
