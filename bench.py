@@ -604,7 +604,7 @@ def measure_config(name, dev, peaks, steps=10, warmup=3, kernel="auto"):
 
 
 def measure_backward(wl, dev, steps):
-    """The backward pass on the workload (BLOCK 128, no permutation): device
+    """The backward pass on the workload (no permutation, 16-bit): device
     time of one block_sparse_attention_backward call (Delta, dQ, dK / dV
     kernels) with the forward's o / lse and both plans resident, against the
     usual 2.5x-forward flop count (5 GEMMs of the kept blocks)."""
@@ -613,7 +613,7 @@ def measure_backward(wl, dev, steps):
     from blocksparsefa_reorder_b200 import (BlockSparsePlan, block_sparse_attention,
                                             block_sparse_attention_backward, transposed_plan)
 
-    if wl.block != 128 or wl.q_perm is not None or str(wl.dtype) == "torch.float32":
+    if wl.q_perm is not None or str(wl.dtype) == "torch.float32":
         return None
     q, k, v = wl.make_qkv(dev)
     g = torch.Generator(device="cpu").manual_seed(wl.seed + 7)

@@ -8,7 +8,7 @@ block_sparse_attention(q, k, v, block_mask, *, q_perm=None, kv_perm=None, ...)
 BlockSparsePlan(block_mask, block)
     the per-tile list of kept key blocks, built on the GPU, reusable.
 block_sparse_attention_backward(q, k, v, o, lse, dout, *, plan, plan_t, ...)
-    gradients dq, dk, dv (BLOCK 128, bf16 / fp16, D 64 / 128; beyond the
+    gradients dq, dk, dv (BLOCK 64 / 128, bf16 / fp16, D 64 / 128; beyond the
     reference, which has no backward); block_sparse_attention_autograd wraps
     forward and backward as a differentiable op.
 kernels.attn_fwd_block_sparse / attn_fwd_block_sparse_perm

@@ -284,7 +284,7 @@ def block_sparse_attention_backward(q: torch.Tensor, k: torch.Tensor, v: torch.T
     ``o`` and ``lse`` are the forward's output and log2 LSE
     (``return_lse=True``); ``plan`` is the forward's plan and ``plan_t`` the
     plan of the transposed block mask (:func:`transposed_plan`).  bf16 /
-    fp16, D 64 or 128, BLOCK 128, on the tcgen05 kernels; P is recomputed
+    fp16, D 64 or 128, BLOCK 64 or 128, on the tcgen05 kernels; P is recomputed
     from ``lse`` and every gradient row is written by one CTA (no atomics,
     deterministic).  The reference has no backward pass.
     """

@@ -170,8 +170,9 @@ extern "C" int bsa_bwd(const bsa_bwd_args* a, void* stream) {
   const bsa_plan* ps[] = {&a->plan, &a->plan_t};
   for (const bsa_plan* p : ps) {
     if (!p->tile_ptr || !p->tile_col) return BSA_ERR_INVALID_ARG;
-    if (p->block != 128) return BSA_ERR_UNSUPPORTED;
-    if (p->nb != (a->N + 127) / 128) return BSA_ERR_SHAPE;
+    if (p->block != 64 && p->block != 128) return BSA_ERR_UNSUPPORTED;
+    if (p->block != a->plan.block) return BSA_ERR_SHAPE;
+    if (p->nb != (a->N + p->block - 1) / p->block) return BSA_ERR_SHAPE;
     if (!(p->mask_b == 1 || p->mask_b == a->B) || !(p->mask_h == 1 || p->mask_h == a->H)) return BSA_ERR_SHAPE;
   }
   if (!(a->sm_scale > 0.f) || !isfinite(a->sm_scale)) return BSA_ERR_UNSUPPORTED;

@@ -1,5 +1,5 @@
-// Block-sparse attention backward for sm_100a: BLOCK 128, head dim 64 or
-// 128, bf16 / fp16, no token permutation.
+// Block-sparse attention backward for sm_100a: BLOCK 64 or 128, head dim 64
+// or 128, bf16 / fp16, no token permutation.
 //
 // The reference has no backward pass: its kernels write the row log-sum-exp
 // M (triton_kernels/BlockSparse_Naive.py:119-122) and nothing consumes it.
@@ -11,15 +11,20 @@
 // Three kernels, no atomics (every output row is written by one CTA, so the
 // result is deterministic):
 //  * bwd_delta_kernel: Delta per query row;
-//  * bwd_dq_kernel: one CTA per 128-row query tile over the tile's kept key
-//    blocks (the forward's plan): S = Q K^T and dP = dO V^T on tcgen05 into
-//    TMEM, dS by the elementwise warpgroup (written back as 16-bit pairs over
-//    S's first 64 columns), dQ += dS K (A from TMEM, K as the MN-major B);
-//  * bwd_dkdv_kernel: one CTA per 128-key block over the query blocks that
-//    keep it (the plan of the transposed mask): S^T = K Q^T and dP^T =
-//    V dO^T into TMEM, P^T and dS^T by the elementwise warpgroup (the query
-//    rows' LSE and Delta staged in shared memory per step), dV += P^T dO and
-//    dK += dS^T Q (dO and Q as MN-major B operands).
+//  * bwd_dq_kernel: one CTA per 128-row query tile over the tile's plan
+//    entries (kept key blocks of BN keys, one per step): S = Q K^T and
+//    dP = dO V^T on tcgen05 into TMEM, dS by the elementwise warpgroup
+//    (written back as 16-bit pairs over S's first BN/2 columns), dQ += dS K
+//    (A from TMEM, K as the MN-major B).  At BLOCK 64 a tile holds two query
+//    blocks and an entry's flags say which of them keeps it: the other
+//    block's rows get P = 0;
+//  * bwd_dkdv_kernel: one CTA per 128-key tile over the entries of the
+//    transposed mask's plan (query blocks of BN rows that keep a key block
+//    of the tile): S^T = K Q^T and dP^T = V dO^T into TMEM, P^T and dS^T by
+//    the elementwise warpgroup (the query rows' LSE and Delta staged in
+//    shared memory per step; at BLOCK 64 the key rows of a key block the
+//    query block does not keep get P = 0), dV += P^T dO and dK += dS^T Q (dO
+//    and Q as MN-major B operands).
 // Roles per CTA (192 threads): warp 0 one thread, TMA producer; warp 1
 // allocates TMEM and one thread issues the MMAs; warps 2-5, one row per
 // thread (TMEM lane quarter = warp % 4), the elementwise work and the
@@ -53,11 +58,16 @@ struct BwdParams {
   uint64_t wait_ns;
 };
 
-template <int D>
+// BN: the block size; the streamed operand of each kernel (K / V in the dQ
+// kernel, Q / dO in the dK/dV kernel) comes in tiles of BN rows, the
+// resident one (Q / dO, resp. K / V) in 128-row tiles.
+template <int D, int BN>
 struct BwdCfg {
   static constexpr int NCHUNK = D / 64;
   static constexpr int CHUNK = 128 * 128;    // one 64-column chunk of a 128-row tile (128-byte swizzle)
   static constexpr int TILE = 128 * D * 2;   // a 128-row tile of D 16-bit columns
+  static constexpr int SCHUNK = BN * 128;    // one 64-column chunk of a BN-row tile
+  static constexpr int STILE = BN * D * 2;   // a BN-row tile
   static constexpr int BAR_BYTES = 256;
 };
 
@@ -140,12 +150,12 @@ __global__ void __launch_bounds__(256) bwd_delta_kernel(const uint8_t* o, int64_
 // dQ: one CTA per 128-row query tile.
 // TMEM columns: S / dS [0, 128), dP [128, 256), dQ [256, 256 + D).
 // ---------------------------------------------------------------------------
-template <int D, bool BF16>
+template <int D, int BN, bool BF16>
 __global__ void __launch_bounds__(kBwdThreads, 1)
     bwd_dq_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
                   const __grid_constant__ CUtensorMap tmV, const __grid_constant__ CUtensorMap tmDO,
                   const BwdParams p) {
-  using C = BwdCfg<D>;
+  using C = BwdCfg<D, BN>;
   extern __shared__ __align__(1024) uint8_t smem[];
   if (smem_u32(smem) & 1023u) {
     if (threadIdx.x == 0) set_err(p.err, BSA_DEVERR_ALIGN);
@@ -153,9 +163,9 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
   }
   uint8_t* sQ = smem;
   uint8_t* sDO = sQ + C::TILE;
-  uint8_t* sK = sDO + C::TILE;   // [2][TILE]
-  uint8_t* sV = sK + 2 * C::TILE;  // [2][TILE]
-  uint64_t* bars = reinterpret_cast<uint64_t*>(sV + 2 * C::TILE);
+  uint8_t* sK = sDO + C::TILE;      // [2][STILE]
+  uint8_t* sV = sK + 2 * C::STILE;  // [2][STILE]
+  uint64_t* bars = reinterpret_cast<uint64_t*>(sV + 2 * C::STILE);
   uint64_t* q_full = bars;        // Q and dO of the tile landed
   uint64_t* kv_full = bars + 1;   // [2] K_j, V_j landed
   uint64_t* kv_empty = bars + 3;  // [2] dQ_j (the last reader of K_j) completed
@@ -192,13 +202,14 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
-  auto key_block = [&](int j) -> int {
-    int kb = static_cast<int>(static_cast<uint32_t>(p.tile_col[e0 + j]) & 0xFFFFFFu);
-    if (kb >= p.nb) {
+  // plan entry j: (flags << 24) | key block
+  auto entry = [&](int j) -> uint32_t {
+    uint32_t en = static_cast<uint32_t>(p.tile_col[e0 + j]);
+    if (static_cast<int>(en & 0xFFFFFFu) >= p.nb) {
       set_err(p.err, BSA_DEVERR_PLAN);
-      kb = 0;
+      en &= 0xFF000000u;
     }
-    return kb;
+    return en;
   };
 
   if (warp == 0 && lane == 0 && n > 0) {
@@ -216,11 +227,11 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
     for (; j < n; ++j) {
       const int st = j & 1;
       if (j >= 2 && !mbar_wait(&kv_empty[st], ((j >> 1) - 1) & 1, abort_flag, p.err, p.wait_ns)) break;
-      const int kb = key_block(j);
-      mbar_arrive_expect_tx(&kv_full[st], 2 * C::TILE);
+      const int kb = static_cast<int>(entry(j) & 0xFFFFFFu);
+      mbar_arrive_expect_tx(&kv_full[st], 2 * C::STILE);
       for (int c = 0; c < C::NCHUNK; ++c) {
-        tma_load_4d(sK + st * C::TILE + c * C::CHUNK, &tmK, &kv_full[st], c * 64, kb * 128, h, b);
-        tma_load_4d(sV + st * C::TILE + c * C::CHUNK, &tmV, &kv_full[st], c * 64, kb * 128, h, b);
+        tma_load_4d(sK + st * C::STILE + c * C::SCHUNK, &tmK, &kv_full[st], c * 64, kb * BN, h, b);
+        tma_load_4d(sV + st * C::STILE + c * C::SCHUNK, &tmV, &kv_full[st], c * 64, kb * BN, h, b);
       }
     }
     // every load issued lands before the CTA exits
@@ -228,7 +239,7 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
     for (int i = j > 2 ? j - 2 : 0; i < j; ++i) mbar_wait(&kv_full[i & 1], (i >> 1) & 1, nullptr, nullptr, p.wait_ns);
   } else if (warp == 1 && lane == 0 && n > 0) {
     // ------------------------------------------------------------ MMA issuer
-    constexpr uint32_t idesc_s = make_idesc_f16(BF16, 128, 128, false, false);
+    constexpr uint32_t idesc_s = make_idesc_f16(BF16, 128, BN, false, false);
     constexpr uint32_t idesc_dq = make_idesc_f16(BF16, 128, D, false, true);
     const uint32_t q_addr = smem_u32(sQ), do_addr = smem_u32(sDO), k_addr = smem_u32(sK), v_addr = smem_u32(sV);
     bool ok = mbar_wait(q_full, 0, abort_flag, p.err, p.wait_ns);
@@ -238,24 +249,27 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
       tc_fence_after();
 #pragma unroll
       for (int kk = 0; kk < D / 16; ++kk) {
-        const uint32_t off = (kk >> 2) * C::CHUNK + (kk & 3) * 32;
-        tc_mma_ss(tmem, make_sw128_desc(q_addr + off, 16, 1024), make_sw128_desc(k_addr + st * C::TILE + off, 16, 1024),
-                  idesc_s, kk > 0 ? 1u : 0u);
+        const uint32_t off = (kk & 3) * 32;
+        tc_mma_ss(tmem, make_sw128_desc(q_addr + (kk >> 2) * C::CHUNK + off, 16, 1024),
+                  make_sw128_desc(k_addr + st * C::STILE + (kk >> 2) * C::SCHUNK + off, 16, 1024), idesc_s,
+                  kk > 0 ? 1u : 0u);
       }
 #pragma unroll
       for (int kk = 0; kk < D / 16; ++kk) {
-        const uint32_t off = (kk >> 2) * C::CHUNK + (kk & 3) * 32;
-        tc_mma_ss(tmem + 128, make_sw128_desc(do_addr + off, 16, 1024),
-                  make_sw128_desc(v_addr + st * C::TILE + off, 16, 1024), idesc_s, kk > 0 ? 1u : 0u);
+        const uint32_t off = (kk & 3) * 32;
+        tc_mma_ss(tmem + 128, make_sw128_desc(do_addr + (kk >> 2) * C::CHUNK + off, 16, 1024),
+                  make_sw128_desc(v_addr + st * C::STILE + (kk >> 2) * C::SCHUNK + off, 16, 1024), idesc_s,
+                  kk > 0 ? 1u : 0u);
       }
       tc_commit(s_full);
       if (!(ok = mbar_wait(ds_ready, j & 1, abort_flag, p.err, p.wait_ns))) break;
       tc_fence_after();
-      // dQ += dS K: dS in the first 64 columns of S's TMEM, K_j MN-major (N = D)
+      // dQ += dS K: dS in the first BN/2 columns of S's TMEM, K_j MN-major (N = D)
 #pragma unroll
-      for (int kk = 0; kk < 128 / 16; ++kk)
-        tc_mma_ts(tmem + 256, tmem + kk * 8, make_sw128_desc(k_addr + st * C::TILE + kk * 16 * 128, C::CHUNK, 1024),
-                  idesc_dq, (j > 0 || kk > 0) ? 1u : 0u);
+      for (int kk = 0; kk < BN / 16; ++kk)
+        tc_mma_ts(tmem + 256, tmem + kk * 8,
+                  make_sw128_desc(k_addr + st * C::STILE + kk * 16 * 128, C::SCHUNK, 1024), idesc_dq,
+                  (j > 0 || kk > 0) ? 1u : 0u);
       tc_commit(&kv_empty[st]);
     }
     tc_commit(done);
@@ -279,9 +293,13 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
       for (int j = 0; j < n; ++j) {
         if (!(ok = ok && __all_sync(0xffffffffu, mbar_wait(s_full, j & 1, abort_flag, p.err, p.wait_ns)))) break;
         tc_fence_after();
-        const int kvalid = p.N - key_block(j) * 128;  // keys at or past N: P = 0
+        const uint32_t en = entry(j);
+        // keys at or past N, and at BLOCK 64 every key of an entry this row's
+        // query block does not keep: P = 0
+        const int kvalid = ((en >> 24 >> (BN == 64 ? row >> 6 : 0)) & 1u)
+                               ? p.N - static_cast<int>(en & 0xFFFFFFu) * BN : 0;
 #pragma unroll
-        for (int c = 0; c < 4; ++c) {
+        for (int c = 0; c < BN / 32; ++c) {
           uint32_t sv[32], dp[32], ds[16];
           tmem_ld32(lane_base + c * 32, sv);
           tmem_ld32(lane_base + 128 + c * 32, dp);
@@ -321,12 +339,12 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
 // TMEM columns: S^T / P^T [0, 128), dP^T / dS^T [128, 256), dV [256, 256 + D),
 // dK [256 + D, 256 + 2D).
 // ---------------------------------------------------------------------------
-template <int D, bool BF16>
+template <int D, int BN, bool BF16>
 __global__ void __launch_bounds__(kBwdThreads, 1)
     bwd_dkdv_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
                     const __grid_constant__ CUtensorMap tmV, const __grid_constant__ CUtensorMap tmDO,
                     const BwdParams p) {
-  using C = BwdCfg<D>;
+  using C = BwdCfg<D, BN>;
   extern __shared__ __align__(1024) uint8_t smem[];
   if (smem_u32(smem) & 1023u) {
     if (threadIdx.x == 0) set_err(p.err, BSA_DEVERR_ALIGN);
@@ -334,9 +352,9 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
   }
   uint8_t* sK = smem;
   uint8_t* sV = sK + C::TILE;
-  uint8_t* sQ = sV + C::TILE;       // [2][TILE]
-  uint8_t* sDO = sQ + 2 * C::TILE;  // [2][TILE]
-  uint64_t* bars = reinterpret_cast<uint64_t*>(sDO + 2 * C::TILE);
+  uint8_t* sQ = sV + C::TILE;        // [2][STILE]
+  uint8_t* sDO = sQ + 2 * C::STILE;  // [2][STILE]
+  uint64_t* bars = reinterpret_cast<uint64_t*>(sDO + 2 * C::STILE);
   float* col_lse = reinterpret_cast<float*>(reinterpret_cast<uint8_t*>(bars) + C::BAR_BYTES);  // [2][128]
   float* col_dlt = col_lse + 256;                                                                  // [2][128]
   uint64_t* kv_full = bars;       // K and V of the key block landed
@@ -375,13 +393,15 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
-  auto query_block = [&](int i) -> int {
-    int qb = static_cast<int>(static_cast<uint32_t>(p.tile_col[e0 + i]) & 0xFFFFFFu);
-    if (qb >= p.nb) {
+  // entry i of the transposed plan: (flags << 24) | query block; flag bit
+  // 0 / 1 = the tile's first / second key block is kept by that query block
+  auto entry = [&](int i) -> uint32_t {
+    uint32_t en = static_cast<uint32_t>(p.tile_col[e0 + i]);
+    if (static_cast<int>(en & 0xFFFFFFu) >= p.nb) {
       set_err(p.err, BSA_DEVERR_PLAN);
-      qb = 0;
+      en &= 0xFF000000u;
     }
-    return qb;
+    return en;
   };
 
   if (warp == 0 && lane == 0 && n > 0) {
@@ -399,18 +419,18 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
     for (; i < n; ++i) {
       const int st = i & 1;
       if (i >= 2 && !mbar_wait(&qd_empty[st], ((i >> 1) - 1) & 1, abort_flag, p.err, p.wait_ns)) break;
-      const int qb = query_block(i);
-      mbar_arrive_expect_tx(&qd_full[st], 2 * C::TILE);
+      const int qb = static_cast<int>(entry(i) & 0xFFFFFFu);
+      mbar_arrive_expect_tx(&qd_full[st], 2 * C::STILE);
       for (int c = 0; c < C::NCHUNK; ++c) {
-        tma_load_4d(sQ + st * C::TILE + c * C::CHUNK, &tmQ, &qd_full[st], c * 64, qb * 128, h, b);
-        tma_load_4d(sDO + st * C::TILE + c * C::CHUNK, &tmDO, &qd_full[st], c * 64, qb * 128, h, b);
+        tma_load_4d(sQ + st * C::STILE + c * C::SCHUNK, &tmQ, &qd_full[st], c * 64, qb * BN, h, b);
+        tma_load_4d(sDO + st * C::STILE + c * C::SCHUNK, &tmDO, &qd_full[st], c * 64, qb * BN, h, b);
       }
     }
     mbar_wait(kv_full, 0, nullptr, nullptr, p.wait_ns);
     for (int k = i > 2 ? i - 2 : 0; k < i; ++k) mbar_wait(&qd_full[k & 1], (k >> 1) & 1, nullptr, nullptr, p.wait_ns);
   } else if (warp == 1 && lane == 0 && n > 0) {
     // ------------------------------------------------------------ MMA issuer
-    constexpr uint32_t idesc_s = make_idesc_f16(BF16, 128, 128, false, false);
+    constexpr uint32_t idesc_s = make_idesc_f16(BF16, 128, BN, false, false);
     constexpr uint32_t idesc_acc = make_idesc_f16(BF16, 128, D, false, true);
     const uint32_t k_addr = smem_u32(sK), v_addr = smem_u32(sV), q_addr = smem_u32(sQ), do_addr = smem_u32(sDO);
     bool ok = mbar_wait(kv_full, 0, abort_flag, p.err, p.wait_ns);
@@ -420,28 +440,31 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
       tc_fence_after();
 #pragma unroll
       for (int kk = 0; kk < D / 16; ++kk) {
-        const uint32_t off = (kk >> 2) * C::CHUNK + (kk & 3) * 32;
-        tc_mma_ss(tmem, make_sw128_desc(k_addr + off, 16, 1024), make_sw128_desc(q_addr + st * C::TILE + off, 16, 1024),
-                  idesc_s, kk > 0 ? 1u : 0u);
+        const uint32_t off = (kk & 3) * 32;
+        tc_mma_ss(tmem, make_sw128_desc(k_addr + (kk >> 2) * C::CHUNK + off, 16, 1024),
+                  make_sw128_desc(q_addr + st * C::STILE + (kk >> 2) * C::SCHUNK + off, 16, 1024), idesc_s,
+                  kk > 0 ? 1u : 0u);
       }
 #pragma unroll
       for (int kk = 0; kk < D / 16; ++kk) {
-        const uint32_t off = (kk >> 2) * C::CHUNK + (kk & 3) * 32;
-        tc_mma_ss(tmem + 128, make_sw128_desc(v_addr + off, 16, 1024),
-                  make_sw128_desc(do_addr + st * C::TILE + off, 16, 1024), idesc_s, kk > 0 ? 1u : 0u);
+        const uint32_t off = (kk & 3) * 32;
+        tc_mma_ss(tmem + 128, make_sw128_desc(v_addr + (kk >> 2) * C::CHUNK + off, 16, 1024),
+                  make_sw128_desc(do_addr + st * C::STILE + (kk >> 2) * C::SCHUNK + off, 16, 1024), idesc_s,
+                  kk > 0 ? 1u : 0u);
       }
       tc_commit(s_full);
       if (!(ok = mbar_wait(pt_ready, i & 1, abort_flag, p.err, p.wait_ns))) break;
       tc_fence_after();
       // dV += P^T dO_i, dK += dS^T Q_i (P^T, dS^T as 16-bit pairs in TMEM; dO_i, Q_i MN-major, N = D)
 #pragma unroll
-      for (int kk = 0; kk < 128 / 16; ++kk)
-        tc_mma_ts(tmem + 256, tmem + kk * 8, make_sw128_desc(do_addr + st * C::TILE + kk * 16 * 128, C::CHUNK, 1024),
-                  idesc_acc, (i > 0 || kk > 0) ? 1u : 0u);
+      for (int kk = 0; kk < BN / 16; ++kk)
+        tc_mma_ts(tmem + 256, tmem + kk * 8,
+                  make_sw128_desc(do_addr + st * C::STILE + kk * 16 * 128, C::SCHUNK, 1024), idesc_acc,
+                  (i > 0 || kk > 0) ? 1u : 0u);
 #pragma unroll
-      for (int kk = 0; kk < 128 / 16; ++kk)
+      for (int kk = 0; kk < BN / 16; ++kk)
         tc_mma_ts(tmem + 256 + D, tmem + 128 + kk * 8,
-                  make_sw128_desc(q_addr + st * C::TILE + kk * 16 * 128, C::CHUNK, 1024), idesc_acc,
+                  make_sw128_desc(q_addr + st * C::STILE + kk * 16 * 128, C::SCHUNK, 1024), idesc_acc,
                   (i > 0 || kk > 0) ? 1u : 0u);
       tc_commit(&qd_empty[st]);
     }
@@ -466,18 +489,23 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
       bool ok = true;
       for (int i = 0; i < n; ++i) {
         // the query rows' LSE and Delta for this step (rows past N: P = 0)
-        const int qrow = query_block(i) * 128 + row;
+        const uint32_t en = entry(i);
+        const int qrow = static_cast<int>(en & 0xFFFFFFu) * BN + row;
         float* lb = col_lse + (i & 1) * 128;
         float* db = col_dlt + (i & 1) * 128;
-        lb[row] = qrow < p.N ? -__ldg(&p.lse[base + qrow]) : -INFINITY;
-        db[row] = qrow < p.N ? __ldg(&p.delta[base + qrow]) : 0.f;
+        if (row < BN) {
+          lb[row] = qrow < p.N ? -__ldg(&p.lse[base + qrow]) : -INFINITY;
+          db[row] = qrow < p.N ? __ldg(&p.delta[base + qrow]) : 0.f;
+        }
+        // at BLOCK 64: a key row of the tile's block that this query block does not keep gets P = 0
+        const bool act = BN == 128 || ((en >> 24 >> (row >> 6)) & 1u) != 0;
         // (a warp whose wait failed keeps taking part in this barrier, which
         // has no time limit, and skips the rest of each step)
         ew_bar_sync();
         if (!(ok = ok && __all_sync(0xffffffffu, mbar_wait(s_full, i & 1, abort_flag, p.err, p.wait_ns)))) continue;
         tc_fence_after();
 #pragma unroll
-        for (int c = 0; c < 4; ++c) {
+        for (int c = 0; c < BN / 32; ++c) {
           uint32_t sv[32], dp[32], pt[16], ds[16];
           tmem_ld32(lane_base + c * 32, sv);
           tmem_ld32(lane_base + 128 + c * 32, dp);
@@ -485,8 +513,8 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
 #pragma unroll
           for (int k = 0; k < 32; k += 2) {
             const int q = c * 32 + k;
-            const float p0 = ex2_approx(fmaf(__uint_as_float(sv[k]), p.scale_log2, lb[q]));
-            const float p1 = ex2_approx(fmaf(__uint_as_float(sv[k + 1]), p.scale_log2, lb[q + 1]));
+            const float p0 = act ? ex2_approx(fmaf(__uint_as_float(sv[k]), p.scale_log2, lb[q])) : 0.f;
+            const float p1 = act ? ex2_approx(fmaf(__uint_as_float(sv[k + 1]), p.scale_log2, lb[q + 1])) : 0.f;
             pt[k / 2] = pack2<BF16>(p0, p1);
             ds[k / 2] = pack2<BF16>(p0 * (__uint_as_float(dp[k]) - db[q]), p1 * (__uint_as_float(dp[k + 1]) - db[q + 1]));
           }
@@ -515,28 +543,34 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
   }
 }
 
-template <int D, bool BF16>
+template <int D, int BN, bool BF16>
 int launch_bwd_t(const bsa_bwd_args* a, cudaStream_t st) {
-  using C = BwdCfg<D>;
-  constexpr int kSmemDq = 6 * C::TILE + C::BAR_BYTES + 1024;
-  constexpr int kSmemDkdv = 6 * C::TILE + C::BAR_BYTES + 2048 + 1024;
+  using C = BwdCfg<D, BN>;
+  constexpr int kSmemDq = 2 * C::TILE + 4 * C::STILE + C::BAR_BYTES;
+  constexpr int kSmemDkdv = 2 * C::TILE + 4 * C::STILE + C::BAR_BYTES + 2048;
   static_assert(kSmemDkdv <= 232448, "shared memory budget");
   static std::atomic<bool> attr_set[64] = {};
   int dev = 0;
   BSA_CUDA_CHECK(cudaGetDevice(&dev));
   if (dev < 0 || dev >= 64) return BSA_ERR_DEVICE;
   if (!attr_set[dev].load(std::memory_order_acquire)) {
-    BSA_CUDA_CHECK(cudaFuncSetAttribute(bwd_dq_kernel<D, BF16>, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemDq));
     BSA_CUDA_CHECK(
-        cudaFuncSetAttribute(bwd_dkdv_kernel<D, BF16>, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemDkdv));
+        cudaFuncSetAttribute(bwd_dq_kernel<D, BN, BF16>, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemDq));
+    BSA_CUDA_CHECK(
+        cudaFuncSetAttribute(bwd_dkdv_kernel<D, BN, BF16>, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemDkdv));
     attr_set[dev].store(true, std::memory_order_release);
   }
-  CUtensorMap mq, mk, mv, mdo;
+  // 128-row tiles of the resident operands, BN-row tiles of the streamed ones
+  CUtensorMap mq, mk, mv, mdo, mq_s, mk_s, mv_s, mdo_s;
   int r;
   if ((r = make_tensor_map_4d(&mq, a->q, a->B, a->H, a->N, D, BF16, 128))) return r;
   if ((r = make_tensor_map_4d(&mk, a->k, a->B, a->H, a->N, D, BF16, 128))) return r;
   if ((r = make_tensor_map_4d(&mv, a->v, a->B, a->H, a->N, D, BF16, 128))) return r;
   if ((r = make_tensor_map_4d(&mdo, a->dout, a->B, a->H, a->N, D, BF16, 128))) return r;
+  if ((r = make_tensor_map_4d(&mq_s, a->q, a->B, a->H, a->N, D, BF16, BN))) return r;
+  if ((r = make_tensor_map_4d(&mk_s, a->k, a->B, a->H, a->N, D, BF16, BN))) return r;
+  if ((r = make_tensor_map_4d(&mv_s, a->v, a->B, a->H, a->N, D, BF16, BN))) return r;
+  if ((r = make_tensor_map_4d(&mdo_s, a->dout, a->B, a->H, a->N, D, BF16, BN))) return r;
 
   const int64_t rows = static_cast<int64_t>(a->B) * a->H * a->N;
   bwd_delta_kernel<BF16><<<static_cast<unsigned>((rows + 7) / 8), 256, 0, st>>>(
@@ -560,12 +594,13 @@ int launch_bwd_t(const bsa_bwd_args* a, cudaStream_t st) {
   p.mask_b = a->plan.mask_b;
   p.mask_h = a->plan.mask_h;
   p.nb = a->plan.nb;
-  p.T = a->plan.nb;  // BLOCK 128: one block row per tile
+  p.T = tiles_per_row(a->plan.nb, BN);
   p.out = static_cast<uint8_t*>(a->dq.data);
   p.os_b = a->dq.stride_b;
   p.os_h = a->dq.stride_h;
   p.os_n = a->dq.stride_n;
-  bwd_dq_kernel<D, BF16><<<static_cast<unsigned>(a->B * a->H * p.T), kBwdThreads, kSmemDq, st>>>(mq, mk, mv, mdo, p);
+  bwd_dq_kernel<D, BN, BF16>
+      <<<static_cast<unsigned>(a->B * a->H * p.T), kBwdThreads, kSmemDq, st>>>(mq, mk_s, mv_s, mdo, p);
   BSA_CUDA_CHECK(cudaGetLastError());
 
   p.tile_ptr = a->plan_t.tile_ptr;
@@ -573,7 +608,7 @@ int launch_bwd_t(const bsa_bwd_args* a, cudaStream_t st) {
   p.mask_b = a->plan_t.mask_b;
   p.mask_h = a->plan_t.mask_h;
   p.nb = a->plan_t.nb;
-  p.T = a->plan_t.nb;
+  p.T = tiles_per_row(a->plan_t.nb, BN);
   p.out = static_cast<uint8_t*>(a->dk.data);
   p.os_b = a->dk.stride_b;
   p.os_h = a->dk.stride_h;
@@ -582,8 +617,8 @@ int launch_bwd_t(const bsa_bwd_args* a, cudaStream_t st) {
   p.os2_b = a->dv.stride_b;
   p.os2_h = a->dv.stride_h;
   p.os2_n = a->dv.stride_n;
-  bwd_dkdv_kernel<D, BF16>
-      <<<static_cast<unsigned>(a->B * a->H * p.T), kBwdThreads, kSmemDkdv, st>>>(mq, mk, mv, mdo, p);
+  bwd_dkdv_kernel<D, BN, BF16>
+      <<<static_cast<unsigned>(a->B * a->H * p.T), kBwdThreads, kSmemDkdv, st>>>(mq_s, mk, mv, mdo_s, p);
   BSA_CUDA_CHECK(cudaGetLastError());
   return BSA_OK;
 }
@@ -592,8 +627,14 @@ int launch_bwd_t(const bsa_bwd_args* a, cudaStream_t st) {
 
 int launch_attn_bwd(const bsa_bwd_args* a, cudaStream_t st) {
   const bool bf16 = a->dtype == BSA_DTYPE_BF16;
-  if (a->D == 128) return bf16 ? launch_bwd_t<128, true>(a, st) : launch_bwd_t<128, false>(a, st);
-  if (a->D == 64) return bf16 ? launch_bwd_t<64, true>(a, st) : launch_bwd_t<64, false>(a, st);
+#define BSA_BWD_CASE(D_, BN_)                                                                  \
+  if (a->D == D_ && a->plan.block == BN_)                                                     \
+    return bf16 ? launch_bwd_t<D_, BN_, true>(a, st) : launch_bwd_t<D_, BN_, false>(a, st);
+  BSA_BWD_CASE(128, 128)
+  BSA_BWD_CASE(64, 128)
+  BSA_BWD_CASE(128, 64)
+  BSA_BWD_CASE(64, 64)
+#undef BSA_BWD_CASE
   return BSA_ERR_UNSUPPORTED;
 }
 

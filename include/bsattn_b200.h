@@ -211,8 +211,8 @@ BSA_API int bsa_fwd_reordered(const bsa_fwd_args* args, const void* q_perm, cons
 
 /* Backward pass (gradients of bsa_fwd), beyond the reference, whose kernels
  * write the row LSE M (triton_kernels/BlockSparse_Naive.py:119-122) but have
- * no backward.  tcgen05 path only: bf16 / fp16, D 64 or 128, BLOCK 128, no
- * token permutation, 16-byte aligned rows.  From dout and the forward's o
+ * no backward.  tcgen05 path only: bf16 / fp16, D 64 or 128, BLOCK 64 or
+ * 128 (both plans of one BLOCK), no token permutation, 16-byte aligned rows.  From dout and the forward's o
  * and lse it writes dq = sm_scale dS K, dk = sm_scale dS^T Q, dv = P^T dout
  * (P recomputed from lse, dS = P o (dout V^T - rowsum(dout o o))), each
  * output row by one CTA (deterministic, no atomics).

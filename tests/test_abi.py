@@ -125,7 +125,7 @@ def test_bwd_rejects_invalid_arguments_on_the_host():
     assert L.bsa_bwd(None, None) == 1
     assert L.bsa_bwd(ctypes.byref(_bwd_args(dtype=_lib.DTYPE_F32)), None) == 3   # f16 / bf16 only
     assert L.bsa_bwd(ctypes.byref(_bwd_args(D=96)), None) == 5                   # D 64 / 128 only
-    assert L.bsa_bwd(ctypes.byref(_bwd_args(block=64, nb=4)), None) == 5         # BLOCK 128 only
+    assert L.bsa_bwd(ctypes.byref(_bwd_args(block=32, nb=8)), None) == 5         # BLOCK 64 / 128 only
     assert L.bsa_bwd(ctypes.byref(_bwd_args(nb=3)), None) == 2                   # nb vs N
     assert L.bsa_bwd(ctypes.byref(_bwd_args(lse=None)), None) == 1               # lse required
     assert L.bsa_bwd(ctypes.byref(_bwd_args(delta=None)), None) == 1             # delta workspace required

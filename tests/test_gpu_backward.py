@@ -54,10 +54,14 @@ def _close(a, ref):
     return (a.float() - ref).abs().max().item() <= TOL[a.dtype] * ref.abs().max().item()
 
 
+@pytest.mark.parametrize("block", [128, 64])
 @pytest.mark.parametrize("D,dtype", [(128, torch.bfloat16), (64, torch.float16), (128, torch.float16),
                                      (64, torch.bfloat16)])
-def test_backward_matches_autograd(dev, D, dtype):
-    B, H, block = 1, 2, 128
+def test_backward_matches_autograd(dev, D, dtype, block):
+    """Per-head masks with a query block that keeps nothing and a key block
+    no query block keeps, a partial last block; at BLOCK 64 the 128-row tiles
+    (and 128-key tiles of the dK/dV kernel) hold blocks kept by one half only."""
+    B, H = 1, 2
     N = 128 * 6 - 40  # a partial last block
     nb = (N + block - 1) // block
     mask = _mask(H, nb, seed=D)
@@ -93,6 +97,25 @@ def test_backward_many_tiles_and_broadcast_mask(dev):
     mask[..., np.arange(nb), np.arange(nb)] = True
     g = torch.Generator(device="cpu").manual_seed(6)
     q, k, v, dout = (torch.randn(B, H, N, D, generator=g).to(torch.bfloat16).to(dev) for _ in range(4))
+    m = torch.from_numpy(mask).to(dev)
+    plan = BlockSparsePlan(m, block)
+    o, lse = block_sparse_attention(q, k, v, plan=plan, return_lse=True, kernel="tcgen05")
+    dq, dk, dv = block_sparse_attention_backward(q, k, v, o, lse, dout, plan=plan, plan_t=transposed_plan(plan, m),
+                                                 check_errors=True)
+    rq, rk, rv = _reference(q, k, v, mask, block, 1.0 / math.sqrt(D), dout)
+    assert _close(dq, rq) and _close(dk, rk) and _close(dv, rv)
+
+
+def test_backward_block64_causal_fp16(dev):
+    """The density sweep's kind of mask (fp16, BLOCK 64, causal with the
+    diagonal kept, below-diagonal blocks at p = 0.3) over B 2 H 3."""
+    B, H, N, D, block = 2, 3, 64 * 24, 128, 64
+    nb = N // block
+    rng = np.random.default_rng(12)
+    mask = np.tril(rng.random((1, 1, nb, nb)) < 0.3)
+    mask[..., np.arange(nb), np.arange(nb)] = True
+    g = torch.Generator(device="cpu").manual_seed(13)
+    q, k, v, dout = (torch.randn(B, H, N, D, generator=g).to(torch.float16).to(dev) for _ in range(4))
     m = torch.from_numpy(mask).to(dev)
     plan = BlockSparsePlan(m, block)
     o, lse = block_sparse_attention(q, k, v, plan=plan, return_lse=True, kernel="tcgen05")
