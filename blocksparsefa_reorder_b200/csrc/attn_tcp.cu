@@ -568,17 +568,21 @@ __global__ void __launch_bounds__(kThreadsP, 1)
         }
         uint32_t pr[HB / 2];
         if (any) {
+          // this thread's HB keys lie in one entry of the step (HB divides BN)
+          const int u = sub * HB / BN;
+          const bool act_u = C::SUB == 1 || u == 0 ? act[0] : act[C::SUB - 1];
           if (need_mask) {
-            // this thread's HB keys lie in one entry of the step (HB divides BN)
-            const int u = sub * HB / BN;
-            const bool act_u = C::SUB == 1 || u == 0 ? act[0] : act[C::SUB - 1];
+            // keys at or past N of a kept entry (an entry this row's block
+            // does not keep is handled whole by softmax_block_split)
             const int kvalid_u = C::SUB == 1 || u == 0 ? kvalid[0] : kvalid[C::SUB - 1];
             const int key0 = sub * HB - u * BN;  // key of sr[0] within that entry
+            if (__any_sync(0xffffffffu, act_u && key0 + HB > kvalid_u)) {
 #pragma unroll
-            for (int i = 0; i < HB; ++i)
-              if (!act_u || key0 + i >= kvalid_u) sr[i] = __float_as_uint(-INFINITY);
+              for (int i = 0; i < HB; ++i)
+                if (key0 + i >= kvalid_u) sr[i] = __float_as_uint(-INFINITY);
+            }
           }
-          const float alpha = softmax_block_split<HB, BF16>(sr, pr, p.scale_log2, m_run, l_run);
+          const float alpha = softmax_block_split<HB, BF16>(sr, pr, p.scale_log2, m_run, l_run, act_u);
           if (__any_sync(0xffffffffu, alpha != 1.f)) {
             // O holds the sum up to block j-1 of this tile: wait for that PV, rescale in TMEM.
             if (!(ok = __all_sync(0xffffffffu,

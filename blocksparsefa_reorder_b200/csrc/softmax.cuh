@@ -116,25 +116,30 @@ __device__ __forceinline__ float softmax_block(const uint32_t (&sr)[BN], uint32_
 // max and the redo run warp-wide when any row of the warp needs them (a row
 // redone without need gets the same reference point or a larger one, and
 // alpha rescales its O and l either way).
+// `active` false: none of this thread's scores is kept (at BLOCK 64, an
+// entry the row's query block does not keep): its P is exactly 0 (the
+// exponent's reference is -inf) and its scores take no part in the max,
+// without masking each score.
 template <int BN, bool BF16>
 __device__ __forceinline__ float softmax_block_split(const uint32_t (&sr)[BN], uint32_t (&pr)[BN / 2],
-                                                     float scale_log2, float& m_run, float& l_run) {
+                                                     float scale_log2, float& m_run, float& l_run,
+                                                     bool active = true) {
   if (__any_sync(0xffffffffu, m_run == -INFINITY)) {
-    float mx = row_max<BN>(sr);
+    float mx = active ? row_max<BN>(sr) : -INFINITY;
     mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 16));
     if (m_run == -INFINITY) m_run = mx * scale_log2;
   }
-  float ls = exp_block<BN, BF16>(sr, pr, scale_log2, -m_run);
+  float ls = exp_block<BN, BF16>(sr, pr, scale_log2, active ? -m_run : -INFINITY);
   ls += __shfl_xor_sync(0xffffffffu, ls, 16);
   float alpha = 1.f;
   if (__any_sync(0xffffffffu, !(ls <= ref_slack<BF16>()))) {
-    float mx = row_max<BN>(sr);
+    float mx = active ? row_max<BN>(sr) : -INFINITY;
     mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 16));
     const float m_new = fmaxf(m_run, mx * scale_log2);
     alpha = ex2_approx(m_run - m_new);
     l_run *= alpha;
     m_run = m_new;
-    ls = exp_block<BN, BF16>(sr, pr, scale_log2, -m_run);
+    ls = exp_block<BN, BF16>(sr, pr, scale_log2, active ? -m_run : -INFINITY);
     ls += __shfl_xor_sync(0xffffffffu, ls, 16);
   }
   l_run += ls;
