@@ -10,7 +10,7 @@
 //   dQ = sm_scale dS K,  dK = sm_scale dS^T Q,  dV = P^T dO
 // Three kernels, no atomics (every output row is written by one CTA, so the
 // result is deterministic):
-//  * bwd_delta_kernel: Delta per query row;
+//  * bwd_delta_kernel: Delta per query row (16-byte loads);
 //  * bwd_dq_kernel: one CTA per 128-row query tile over the tile's plan
 //    entries (kept key blocks of BN keys, one per step): S = Q K^T and
 //    dP = dO V^T on tcgen05 into TMEM, dS by the elementwise warpgroup
@@ -111,24 +111,25 @@ __device__ __forceinline__ void zero_row(uint8_t* row) {
   for (int i = 0; i < D / 8; ++i) reinterpret_cast<uint4*>(row)[i] = make_uint4(0, 0, 0, 0);
 }
 
-// Delta[b, h, n] = sum_d dO[n, d] * O[n, d] in fp32, one warp per row.
-template <bool BF16>
+// Delta[b, h, n] = sum_d dO[n, d] * O[n, d] in fp32: each row read by D / 8
+// lanes with 16-byte loads (two rows per warp at D = 128, four at D = 64).
+template <bool BF16, int D>
 __global__ void __launch_bounds__(256) bwd_delta_kernel(const uint8_t* o, int64_t o_b, int64_t o_h, int64_t o_n,
                                                         const uint8_t* dout, int64_t d_b, int64_t d_h, int64_t d_n,
-                                                        float* delta, int B, int H, int N, int D) {
-  const int64_t r = static_cast<int64_t>(blockIdx.x) * 8 + (threadIdx.x >> 5);
+                                                        float* delta, int B, int H, int N) {
+  constexpr int LPR = D / 8;  // lanes per row
   const int lane = threadIdx.x & 31;
-  if (r >= static_cast<int64_t>(B) * H * N) return;
-  const int64_t bh = r / N, n = r - bh * N, b = bh / H, h = bh - b * H;
-  const uint8_t* orow = o + 2 * (b * o_b + h * o_h + n * o_n);
-  const uint8_t* drow = dout + 2 * (b * d_b + h * d_h + n * d_n);
+  const int64_t r = (static_cast<int64_t>(blockIdx.x) * 8 + (threadIdx.x >> 5)) * (32 / LPR) + lane / LPR;
+  const bool live = r < static_cast<int64_t>(B) * H * N;
   float acc = 0.f;
-  for (int d = lane * 4; d < D; d += 128) {
-    const uint2 ov = *reinterpret_cast<const uint2*>(orow + 2 * d);
-    const uint2 dv = *reinterpret_cast<const uint2*>(drow + 2 * d);
-    const uint32_t ow[2] = {ov.x, ov.y}, dw[2] = {dv.x, dv.y};
+  if (live) {
+    const int64_t bh = r / N, n = r - bh * N, b = bh / H, h = bh - b * H;
+    const int d = (lane % LPR) * 8;
+    const uint4 ov = *reinterpret_cast<const uint4*>(o + 2 * (b * o_b + h * o_h + n * o_n + d));
+    const uint4 dv = *reinterpret_cast<const uint4*>(dout + 2 * (b * d_b + h * d_h + n * d_n + d));
+    const uint32_t ow[4] = {ov.x, ov.y, ov.z, ov.w}, dw[4] = {dv.x, dv.y, dv.z, dv.w};
 #pragma unroll
-    for (int k = 0; k < 2; ++k) {
+    for (int k = 0; k < 4; ++k) {
       float o0, o1, d0, d1;
       if constexpr (BF16) {
         o0 = __uint_as_float(ow[k] << 16), o1 = __uint_as_float(ow[k] & 0xFFFF0000u);
@@ -142,8 +143,8 @@ __global__ void __launch_bounds__(256) bwd_delta_kernel(const uint8_t* o, int64_
     }
   }
 #pragma unroll
-  for (int off = 16; off > 0; off >>= 1) acc += __shfl_xor_sync(0xffffffffu, acc, off);
-  if (lane == 0) delta[r] = acc;
+  for (int off = LPR / 2; off > 0; off >>= 1) acc += __shfl_xor_sync(0xffffffffu, acc, off);
+  if (live && lane % LPR == 0) delta[r] = acc;
 }
 
 // ---------------------------------------------------------------------------
@@ -573,10 +574,11 @@ int launch_bwd_t(const bsa_bwd_args* a, cudaStream_t st) {
   if ((r = make_tensor_map_4d(&mdo_s, a->dout, a->B, a->H, a->N, D, BF16, BN))) return r;
 
   const int64_t rows = static_cast<int64_t>(a->B) * a->H * a->N;
-  bwd_delta_kernel<BF16><<<static_cast<unsigned>((rows + 7) / 8), 256, 0, st>>>(
+  const int64_t rows_per_block = 8 * (32 / (D / 8));
+  bwd_delta_kernel<BF16, D><<<static_cast<unsigned>((rows + rows_per_block - 1) / rows_per_block), 256, 0, st>>>(
       static_cast<const uint8_t*>(a->o.data), a->o.stride_b, a->o.stride_h, a->o.stride_n,
       static_cast<const uint8_t*>(a->dout.data), a->dout.stride_b, a->dout.stride_h, a->dout.stride_n, a->delta,
-      a->B, a->H, a->N, D);
+      a->B, a->H, a->N);
   BSA_CUDA_CHECK(cudaGetLastError());
 
   BwdParams p{};
