@@ -582,7 +582,7 @@ def measure_config(name, dev, peaks, steps=10, warmup=3, kernel="auto"):
     out = {
         "workload": describe(wl), "density": round(wl.density, 5), "nnz_blocks": wl.nnz_blocks,
         "kernel": ("attn_simt_kernel" if not tensor else
-                   "attn_tcp_kernel " + ("paired" if wl.block == 64 and tile_entries >= 32 * tiles else
+                   "attn_tcp_kernel " + ("paired" if wl.block == 64 and tile_entries >= 4 * tiles else
                                          "single-block steps" if wl.block == 64 else "BLOCK128")),
         "entries_per_tile": round(tile_entries / tiles, 2),
         "kernel_ms": kern_ms, "step_ms": step_ms, "plan_build_ms": t_plan,

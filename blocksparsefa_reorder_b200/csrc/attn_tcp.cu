@@ -120,9 +120,10 @@ struct TcpParams {
 
 // BLOCK 64: tiles averaging at least this many kept key blocks run the form
 // that takes them in pairs (128-key steps); sparser plans run one block per
-// step, where the shorter steps pipeline better (measured crossover between
-// 27 and 93 kept blocks per tile on causal masks).
-constexpr int kPairMinEntries = 32;
+// step.  Measured on the causal sweep masks, the paired form is faster from
+// 7 kept blocks per tile up (359 vs 320 TF/s at 7, 446-458 vs 366-370 at
+// 26.6); below 4 a tile has so few steps that pairing saves little.
+constexpr int kPairMinEntries = 4;
 
 constexpr int kSmemLimitP = 232448;
 constexpr int kThreadsP = 512;

@@ -470,19 +470,20 @@ def test_long_context_sampled(dev):
         assert np.abs(gl[:, :, r0:r1] - ref_lse[:, :, r0:r1]).max() <= TOL_LSE
 
 
+@pytest.mark.parametrize("density,paired", [(0.05, False), (0.3, True)])
 @pytest.mark.parametrize("D", [64, 128])
-def test_block64_single_form_edges(dev, D):
-    """BLOCK 64 with a sparse plan (tiles average fewer than 32 kept blocks),
-    so the kernel form that runs one kept block per step is the one selected:
-    tiles with an odd number of kept blocks, blocks kept by only one of the
-    tile's two query block rows, a tile whose rows keep disjoint blocks, a
-    partial last key block (N % 64 != 0), and key blocks no query keeps filled
-    with NaN.  (The paired form's edges are covered in test_gpu_configs.py.)"""
+def test_block64_forms_edges(dev, D, density, paired):
+    """BLOCK 64 with a sparse plan (tiles average fewer than 4 kept blocks:
+    the form that runs one kept block per step is selected) and a denser one
+    (the paired form): tiles with an odd number of kept blocks, blocks kept by
+    only one of the tile's two query block rows, a tile whose rows keep
+    disjoint blocks, a partial last key block (N % 64 != 0), and key blocks no
+    query keeps filled with NaN."""
     B, H, block = 1, 3, 64
     N = 64 * 13 + 23
     nb = (N + block - 1) // block
     rng = np.random.default_rng(D)
-    mask = rng.random((1, H, nb, nb)) < 0.3
+    mask = rng.random((1, H, nb, nb)) < density
     mask[..., np.arange(nb), np.arange(nb)] = True
     mask[:, 0, 2, :] = False                       # rows 2 and 3 (one tile) keep disjoint blocks
     mask[:, 0, 3, :] = False
@@ -497,7 +498,8 @@ def test_block64_single_form_edges(dev, D):
     k[:, 2, 11 * block:12 * block] = float("nan")
     v[:, 2, 11 * block:12 * block] = float("nan")
     plan = BlockSparsePlan(torch.from_numpy(mask).to(dev), block)
-    assert plan.nnz_entries() < 32 * plan.mask_b * plan.mask_h * plan.tiles_per_row  # the single form runs
+    # the form the kernels select from the plan's entry total (4 per tile)
+    assert (plan.nnz_entries() >= 4 * plan.mask_b * plan.mask_h * plan.tiles_per_row) == paired
     o, lse = block_sparse_attention(q, k, v, plan=plan, kernel="tcgen05", return_lse=True, check_errors=True)
     kc, vc = k.clone(), v.clone()
     kc[:, 2, 11 * block:12 * block] = 0
