@@ -40,16 +40,16 @@
 // Buffers: S double-buffered in TMEM by global block counter g (S_g in
 // buffer g&1); O double-buffered by non-empty-tile counter e (O_e in buffer
 // e&1); Q double-buffered in shared memory by e; K and V in rings of KS and
-// VS stages; a step is 128 keys (one kept block at BLOCK 128, two at
-// BLOCK 64).  TMEM columns: S0 [0,BS), S1 [BS,2BS), O0 [2BS,2BS+D),
-// O1 [2BS+D,2BS+2D), BS = 128.
+// VS stages; a step is BS keys: one kept block at BLOCK 128, two in the
+// paired BLOCK-64 form (BS = 128), one in the single BLOCK-64 form (BS = 64).
+// TMEM columns: S0 [0,BS), S1 [BS,2BS), O0 [2BS,2BS+D), O1 [2BS+D,2BS+2D).
 // Ordering facts (one thread's tcgen05.mma operations execute in issue order
 // and tcgen05.commit tracks every earlier one):
 //  * S_g+2 reuses S_g's TMEM and is issued after PV_g, which reads P_g there;
 //  * S_g complete implies PV_g-2 complete, and PV_g-1 completes before any
 //    later MMA: the softmax's rescale of O waits step_done of PV_g-1;
-//  * S_g complete (s_full, seen by softmax warp 0, which then arrives on
-//    k_empty) frees K_g's stage; the commit after PV_g (step_done[g % 4])
+//  * S_g complete (s_full, seen by the first softmax warp, warp 4, which
+//    then arrives on k_empty) frees K_g's stage; the commit after PV_g (step_done[g % 4])
 //    frees V_g's stage and lets a rescale of O go ahead;
 //  * Q_e's buffer is released (q_empty) by a commit after the tile's last S;
 //  * the first PV of tile e+2 waits o_empty[e&1]: the epilogue has read O_e.
