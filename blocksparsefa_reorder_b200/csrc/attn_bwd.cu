@@ -149,7 +149,11 @@ __global__ void __launch_bounds__(256) bwd_delta_kernel(const uint8_t* o, int64_
 
 // ---------------------------------------------------------------------------
 // dQ: one CTA per 128-row query tile.
-// TMEM columns: S / dS [0, 128), dP [128, 256), dQ [256, 256 + D).
+// TMEM columns: S_j / dS_j in [128 (j & 1), +128), dP [256, 384), dQ
+// [384, 384 + D).  S is double-buffered: S_j+1 is computed while the
+// elementwise warpgroup turns S_j and dP_j into dS_j; then dP_j+1 is issued
+// before dQ_j, so the next elementwise step waits for one MMA group, not
+// three.
 // ---------------------------------------------------------------------------
 template <int D, int BN, bool BF16>
 __global__ void __launch_bounds__(kBwdThreads, 1)
@@ -170,10 +174,11 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
   uint64_t* q_full = bars;        // Q and dO of the tile landed
   uint64_t* kv_full = bars + 1;   // [2] K_j, V_j landed
   uint64_t* kv_empty = bars + 3;  // [2] dQ_j (the last reader of K_j) completed
-  uint64_t* s_full = bars + 5;    // S_j and dP_j complete
-  uint64_t* ds_ready = bars + 6;  // 4 elementwise warps wrote dS_j
-  uint64_t* done = bars + 7;      // every MMA complete
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 8);
+  uint64_t* s_full = bars + 5;    // [2] S_j complete, by S buffer j & 1
+  uint64_t* dp_full = bars + 7;   // dP_j complete
+  uint64_t* ds_ready = bars + 8;  // 4 elementwise warps wrote dS_j (and are done with dP_j)
+  uint64_t* done = bars + 9;      // every MMA complete
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 10);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -189,7 +194,8 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
       mbar_init(&kv_full[i], 1);
       mbar_init(&kv_empty[i], 1);
     }
-    mbar_init(s_full, 1);
+    for (int i = 0; i < 2; ++i) mbar_init(&s_full[i], 1);
+    mbar_init(dp_full, 1);
     mbar_init(ds_ready, 4);
     mbar_init(done, 1);
     *abort_flag = 0;
@@ -203,6 +209,7 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
+  constexpr uint32_t kDP = 256, kDQ = 384;  // TMEM columns of dP and dQ
   // plan entry j: (flags << 24) | key block
   auto entry = [&](int j) -> uint32_t {
     uint32_t en = static_cast<uint32_t>(p.tile_col[e0 + j]);
@@ -243,32 +250,52 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
     constexpr uint32_t idesc_s = make_idesc_f16(BF16, 128, BN, false, false);
     constexpr uint32_t idesc_dq = make_idesc_f16(BF16, 128, D, false, true);
     const uint32_t q_addr = smem_u32(sQ), do_addr = smem_u32(sDO), k_addr = smem_u32(sK), v_addr = smem_u32(sV);
-    bool ok = mbar_wait(q_full, 0, abort_flag, p.err, p.wait_ns);
-    for (int j = 0; ok && j < n; ++j) {
+    // S_j = Q K_j^T into S buffer j & 1; dP_j = dO V_j^T
+    auto issue_s = [&](int j) {
       const int st = j & 1;
-      if (!(ok = mbar_wait(&kv_full[st], (j >> 1) & 1, abort_flag, p.err, p.wait_ns))) break;
-      tc_fence_after();
 #pragma unroll
       for (int kk = 0; kk < D / 16; ++kk) {
         const uint32_t off = (kk & 3) * 32;
-        tc_mma_ss(tmem, make_sw128_desc(q_addr + (kk >> 2) * C::CHUNK + off, 16, 1024),
+        tc_mma_ss(tmem + st * 128, make_sw128_desc(q_addr + (kk >> 2) * C::CHUNK + off, 16, 1024),
                   make_sw128_desc(k_addr + st * C::STILE + (kk >> 2) * C::SCHUNK + off, 16, 1024), idesc_s,
                   kk > 0 ? 1u : 0u);
       }
+      tc_commit(&s_full[st]);
+    };
+    auto issue_dp = [&](int j) {
+      const int st = j & 1;
 #pragma unroll
       for (int kk = 0; kk < D / 16; ++kk) {
         const uint32_t off = (kk & 3) * 32;
-        tc_mma_ss(tmem + 128, make_sw128_desc(do_addr + (kk >> 2) * C::CHUNK + off, 16, 1024),
+        tc_mma_ss(tmem + kDP, make_sw128_desc(do_addr + (kk >> 2) * C::CHUNK + off, 16, 1024),
                   make_sw128_desc(v_addr + st * C::STILE + (kk >> 2) * C::SCHUNK + off, 16, 1024), idesc_s,
                   kk > 0 ? 1u : 0u);
       }
-      tc_commit(s_full);
+      tc_commit(dp_full);
+    };
+    bool ok = mbar_wait(q_full, 0, abort_flag, p.err, p.wait_ns) && mbar_wait(&kv_full[0], 0, abort_flag, p.err, p.wait_ns);
+    if (ok) {
+      tc_fence_after();
+      issue_s(0);
+      issue_dp(0);
+    }
+    for (int j = 0; ok && j < n; ++j) {
+      const int st = j & 1;
+      // S_j+1 into the other buffer while the elementwise warps work on step j
+      // (that buffer's dS_j-1 was read by dQ_j-1, issued before)
+      if (j + 1 < n) {
+        if (!(ok = mbar_wait(&kv_full[st ^ 1], ((j + 1) >> 1) & 1, abort_flag, p.err, p.wait_ns))) break;
+        tc_fence_after();
+        issue_s(j + 1);
+      }
       if (!(ok = mbar_wait(ds_ready, j & 1, abort_flag, p.err, p.wait_ns))) break;
       tc_fence_after();
-      // dQ += dS K: dS in the first BN/2 columns of S's TMEM, K_j MN-major (N = D)
+      // dP's buffer is free again: dP_j+1 first, so that step j+1 can start
+      if (j + 1 < n) issue_dp(j + 1);
+      // dQ += dS_j K_j: dS in the first BN/2 columns of S buffer j & 1, K_j MN-major (N = D)
 #pragma unroll
       for (int kk = 0; kk < BN / 16; ++kk)
-        tc_mma_ts(tmem + 256, tmem + kk * 8,
+        tc_mma_ts(tmem + kDQ, tmem + st * 128 + kk * 8,
                   make_sw128_desc(k_addr + st * C::STILE + kk * 16 * 128, C::SCHUNK, 1024), idesc_dq,
                   (j > 0 || kk > 0) ? 1u : 0u);
       tc_commit(&kv_empty[st]);
@@ -292,8 +319,12 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
       const float dlt = live ? __ldg(&p.delta[ri]) : 0.f;
       bool ok = true;
       for (int j = 0; j < n; ++j) {
-        if (!(ok = ok && __all_sync(0xffffffffu, mbar_wait(s_full, j & 1, abort_flag, p.err, p.wait_ns)))) break;
+        if (!(ok = ok && __all_sync(0xffffffffu, mbar_wait(&s_full[j & 1], (j >> 1) & 1, abort_flag, p.err,
+                                                              p.wait_ns) &&
+                                                       mbar_wait(dp_full, j & 1, abort_flag, p.err, p.wait_ns))))
+          break;
         tc_fence_after();
+        const uint32_t s_col = (j & 1) * 128;
         const uint32_t en = entry(j);
         // keys at or past N, and at BLOCK 64 every key of an entry this row's
         // query block does not keep: P = 0
@@ -302,8 +333,8 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
 #pragma unroll
         for (int c = 0; c < BN / 32; ++c) {
           uint32_t sv[32], dp[32], ds[16];
-          tmem_ld32(lane_base + c * 32, sv);
-          tmem_ld32(lane_base + 128 + c * 32, dp);
+          tmem_ld32(lane_base + s_col + c * 32, sv);
+          tmem_ld32(lane_base + kDP + c * 32, dp);
           tmem_wait_ld();
 #pragma unroll
           for (int k = 0; k < 32; k += 2) {
@@ -313,7 +344,7 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
             ds[k / 2] = pack2<BF16>(p0 * (__uint_as_float(dp[k]) - dlt), p1 * (__uint_as_float(dp[k + 1]) - dlt));
           }
           // dS columns [16c, 16c + 16) hold S columns already read (chunks <= c)
-          tmem_st16(lane_base + c * 16, ds);
+          tmem_st16(lane_base + s_col + c * 16, ds);
         }
         tmem_wait_st();
         tc_fence_before();
@@ -323,7 +354,7 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
       ok = ok && __all_sync(0xffffffffu, mbar_wait(done, 0, abort_flag, p.err, p.wait_ns));
       if (ok) {
         tc_fence_after();
-        store_acc_row<D, BF16>(lane_base, 256, p.sm_scale, orow, live);
+        store_acc_row<D, BF16>(lane_base, kDQ, p.sm_scale, orow, live);
       }
     }
   }
