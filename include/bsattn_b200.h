@@ -155,7 +155,11 @@ BSA_API int bsa_build_plan_noalloc(const uint8_t* mask, int64_t stride_b, int64_
  * Replaces _attn_fwd_block_sparse (triton_kernels/BlockSparse_Naive.py:68-125)
  * as launched at BlockSparseTriton_Naive.py:142-156: o = softmax over kept
  * blocks of (q k^T * sm_scale) v; rows that keep no block give o = 0 and
- * lse = -inf. */
+ * lse = -inf.  At BLOCK 64 a 128-row tile reads every key block that either
+ * of its two 64-row query blocks keeps, and the rows whose block does not
+ * keep it add 0 x V: the masked blocks contribute exactly nothing when V is
+ * finite in the blocks a tile's other query block keeps (NaN / Inf there
+ * would reach those rows).  BLOCK 128 has no such condition. */
 BSA_API int bsa_fwd(const bsa_fwd_args* args, void* stream);
 
 /* Row gather / scatter along N for every (b, h); D = elements per row:
