@@ -60,6 +60,9 @@ FALLBACK_PEAKS = {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustain
 DTYPE_NAMES = {"torch.bfloat16": "bf16", "torch.float16": "fp16", "torch.float32": "f32"}
 L2_BYTES = 126 * 2**20
 CONFIGS = ["plumbing", "random", "sbm", "headline", "longctx", "sweep_p01", "sweep_p05", "sweep_p20", "sweep_p50"]
+# long context under torchrun: each rank's heads are computed in this many
+# parts, each part's O sent to rank 0 while the next part computes
+GATHER_PARTS = 4
 # DRAM bytes per attention launch from one ncu capture of the same kernel on the
 # same workload (dram__bytes_read.sum + dram__bytes_write.sum), with the
 # command that produced it; --ncu-csv takes the figure from a capture instead.
@@ -669,23 +672,25 @@ def run_ours(args):
     job_flops = wl.flops if strong else per_rank_flops * world
 
     if gather:
-        # long context: each rank's heads in two halves; a half's O goes to
-        # rank 0 (placed at its global head index) while the next half computes
+        # long context: each rank's heads in GATHER_PARTS parts; a part's O
+        # goes to rank 0 (placed at its global head index) while the next
+        # part computes, so only the last part's transfer is exposed
         q, k, v, o = run.sets[0]
         full = torch.empty((units_total, wl.N, wl.D), dtype=q.dtype, device=dev) if rank == 0 else None
 
-        def halves(r):
+        def parts(r):
             U = ranges[r][1] - ranges[r][0]
-            return [(0, U // 2), (U // 2, U)]
+            cut = [U * i // GATHER_PARTS for i in range(GATHER_PARTS + 1)]
+            return [(cut[i], cut[i + 1]) for i in range(GATHER_PARTS)]
 
         def step(i):
             works = []
-            for part in range(2):
-                a, b = halves(rank)[part]
+            for part in range(GATHER_PARTS):
+                a, b = parts(rank)[part]
                 if b > a:
                     block_sparse_attention(q[:, a:b], k[:, a:b], v[:, a:b], plan=run.plan, out=o[:, a:b],
                                            kernel=run.kernel)
-                sizes = [halves(r)[part] for r in range(world)]
+                sizes = [parts(r)[part] for r in range(world)]
                 offs = [ranges[r][0] + sizes[r][0] for r in range(world)]
                 _, w = sharding.gather_units(o[0, a:b], sizes, dst=0, async_op=True, out=full, offsets=offs)
                 works += w
@@ -864,8 +869,8 @@ def run_ours(args):
                     "its block mask); the K steps are replayed from CUDA graphs of %d forwards back to back "
                     "(then single-forward graphs for the remainder), exactly K forwards; the kernel time comes "
                     "from events around single-forward replays" % group if not gather else
-                    "attention forward per half of the rank's heads with the O gather to rank 0 posted after "
-                    "each half (eager calls)",
+                    "attention forward in %d parts of the rank's heads with the O gather to rank 0 posted "
+                    "after each part (eager calls)" % GATHER_PARTS,
             "l2": ("inputs larger than L2: %d input cop%s of q, k, v, o, %d MiB per rank, rotated per step"
                    % (n_copies, "y" if n_copies == 1 else "ies", footprint // 2**20))},
         "roofline": {"bound": "tensor", "achieved": achieved, "peak": peak, "unit": "TFLOP/s",

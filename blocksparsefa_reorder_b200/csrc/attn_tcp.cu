@@ -351,7 +351,13 @@ __global__ void __launch_bounds__(kThreadsP, 1)
         tile_ring[ri].h = h;
         tile_ring[ri].t = t;
         mbar_arrive(&tile_ready[ri]);  // release: the entry is visible to every waiter
-        if (w < 0) break;
+        if (w < 0) {
+          // No more tiles for this CTA: the next kernel on the stream (launched
+          // as a programmatic dependent) may start its set-up on SMs as they
+          // free up; it reads global memory only after this grid completed.
+          allow_dependents();
+          break;
+        }
         if (n == 0) continue;
         const int qb = e & 1;
         if (!p.q_perm) {  // (permuted queries: warps 2-3 gather Q)
