@@ -34,6 +34,10 @@ measured on this GPU (kernel time, TFLOP/s, roofline fractions, measured
 density, a max-abs-error spot check against an fp64 masked softmax on sampled
 query blocks).
 
+At N = 1 the line also carries ``gpu_comparator``: ``torch.compile(
+flex_attention)`` (the reference's FlexAttention backend, library code) on the
+same inputs and block mask on this GPU, with this library's speed-up over it.
+
 ``--impl reference`` times the CPU restatement of the reference's block loop
 (the oracle port: one float32 numpy program per query block, one process per
 host core) on a bounded sample of the same workload, on rank 0 only.
@@ -606,6 +610,54 @@ def measure_config(name, dev, peaks, steps=10, warmup=3, kernel="auto"):
     return out
 
 
+def measure_flex(wl, dev, steps, warmup=5):
+    """GPU comparator on the same B200: ``torch.compile(flex_attention)``
+    with a BlockMask of the workload's block mask, the reference's
+    FlexAttention backend (BlockSparseXF.py:43-63) and the comparator BASELINE
+    names for every configuration.  Library code, not this build: timed with
+    CUDA events over ``steps`` calls after ``warmup``, outputs compared with
+    this library's on the same inputs."""
+    import torch
+    from torch.nn.attention.flex_attention import create_block_mask, flex_attention
+
+    from blocksparsefa_reorder_b200 import BlockSparsePlan, block_sparse_attention
+
+    if wl.q_perm is not None or wl.kv_perm is not None or wl.dtype == torch.float32:
+        return {"skipped": "comparator run on identity-permutation 16-bit workloads only"}
+    q, k, v = wl.make_qkv(dev)
+    bm = torch.from_numpy(wl.mask).to(dev)
+    blk = wl.block
+
+    def mask_mod(b, h, qi, ki):
+        return bm[qi // blk, ki // blk]
+
+    t0 = time.time()
+    block_mask = create_block_mask(mask_mod, None, None, wl.N, wl.N, device=dev, BLOCK_SIZE=blk)
+    fa = torch.compile(flex_attention)
+    o_f = fa(q, k, v, block_mask=block_mask)
+    torch.cuda.synchronize()
+    setup_s = time.time() - t0
+    o = block_sparse_attention(q, k, v, plan=BlockSparsePlan(wl.mask_tensor(dev), blk))
+    diff = (o.float() - o_f.float()).abs().max().item()
+    for _ in range(warmup):
+        fa(q, k, v, block_mask=block_mask)
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(steps):
+        fa(q, k, v, block_mask=block_mask)
+    e1.record()
+    torch.cuda.synchronize()
+    ms = e0.elapsed_time(e1) / steps
+    out = {"impl": "torch.compile(flex_attention) with a BlockMask of the same block mask (BLOCK_SIZE %d)" % blk,
+           "value": wl.flops / (ms * 1e-3) / 1e12, "unit": UNIT, "ms_per_step": ms,
+           "max_abs_diff_vs_this_library": diff, "setup_s": setup_s,
+           "what": "secondary GPU comparator on the same B200; the reference arm stays the CPU path"}
+    del q, k, v, o, o_f, block_mask
+    torch.cuda.empty_cache()
+    return out
+
+
 def measure_backward(wl, dev, steps):
     """The backward pass on the workload (no permutation, 16-bit): device
     time of one block_sparse_attention_backward call (Delta, dQ, dK / dV
@@ -850,6 +902,13 @@ def run_ours(args):
 
     backward = measure_backward(wl, dev, args.steps) if world == 1 and not args.no_backward else None
 
+    gpu_comparator = None
+    if world == 1 and not args.no_gpu_comparator:
+        try:
+            gpu_comparator = measure_flex(wl, dev, args.steps)
+        except Exception as e:  # report, do not hide
+            gpu_comparator = {"error": f"{type(e).__name__}: {e}"}
+
     per_config = None
     if world == 1 and not args.no_per_config:
         per_config = {}
@@ -902,6 +961,11 @@ def run_ours(args):
     }
     if backward is not None:
         line["backward"] = backward
+    if gpu_comparator is not None:
+        ours_ms = ms_step
+        if "ms_per_step" in gpu_comparator:
+            gpu_comparator["this_library_speedup"] = gpu_comparator["ms_per_step"] / ours_ms
+        line["gpu_comparator"] = gpu_comparator
     if per_config is not None:
         line["per_config"] = per_config
     if not args.no_cpu_baseline and world == 1:
@@ -928,6 +992,8 @@ def main(argv=None):
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-per-config", action="store_true")
     ap.add_argument("--no-backward", action="store_true", help="skip the backward-pass measurement")
+    ap.add_argument("--no-gpu-comparator", action="store_true",
+                    help="skip the torch.compile(flex_attention) comparator on the same GPU")
     ap.add_argument("--kernel", default="auto", help="kernel choice passed to block_sparse_attention")
     ap.add_argument("--configs", default=",".join(CONFIGS), help="configurations of the per-config object")
     ap.add_argument("--ncu-csv", default=None, help="ncu raw CSV of the same command: roofline traffic from it")
