@@ -631,21 +631,23 @@ def measure_flex(wl, dev, steps, warmup=5):
     def mask_mod(b, h, qi, ki):
         return bm[qi // blk, ki // blk]
 
+    # its kernel tiles must divide the mask's block (64-blocks need 64 x 64 tiles)
+    opts = {"BLOCK_M": blk, "BLOCK_N": blk} if blk < 128 else None
     t0 = time.time()
     block_mask = create_block_mask(mask_mod, None, None, wl.N, wl.N, device=dev, BLOCK_SIZE=blk)
     fa = torch.compile(flex_attention)
-    o_f = fa(q, k, v, block_mask=block_mask)
+    o_f = fa(q, k, v, block_mask=block_mask, kernel_options=opts)
     torch.cuda.synchronize()
     setup_s = time.time() - t0
     o = block_sparse_attention(q, k, v, plan=BlockSparsePlan(wl.mask_tensor(dev), blk))
     diff = (o.float() - o_f.float()).abs().max().item()
     for _ in range(warmup):
-        fa(q, k, v, block_mask=block_mask)
+        fa(q, k, v, block_mask=block_mask, kernel_options=opts)
     torch.cuda.synchronize()
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     e0.record()
     for _ in range(steps):
-        fa(q, k, v, block_mask=block_mask)
+        fa(q, k, v, block_mask=block_mask, kernel_options=opts)
     e1.record()
     torch.cuda.synchronize()
     ms = e0.elapsed_time(e1) / steps
@@ -917,6 +919,18 @@ def run_ours(args):
                 per_config[name] = measure_config(name, dev, peaks, kernel=args.kernel)
             except Exception as e:  # report, do not hide
                 per_config[name] = {"error": f"{type(e).__name__}: {e}"}
+                continue
+            if args.no_gpu_comparator:
+                continue
+            try:
+                fc = measure_flex(W.make(name), dev, steps=5, warmup=3)
+                if "ms_per_step" in fc:
+                    fc = {"flex_ms": fc["ms_per_step"], "flex_tflops": fc["value"],
+                          "this_library_speedup": fc["ms_per_step"] / per_config[name]["kernel_ms"],
+                          "max_abs_diff": fc["max_abs_diff_vs_this_library"]}
+                per_config[name]["gpu_comparator"] = fc
+            except Exception as e:  # report, do not hide
+                per_config[name]["gpu_comparator"] = {"error": f"{type(e).__name__}: {e}"}
 
     peak = float(peaks.get("bf16_tflops", FALLBACK_PEAKS["bf16_tflops"]))
     achieved = per_rank_flops / (kern_ms * 1e-3) / 1e12
