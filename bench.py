@@ -732,21 +732,16 @@ def run_ours(args):
         q, k, v, o = run.sets[0]
         full = torch.empty((units_total, wl.N, wl.D), dtype=q.dtype, device=dev) if rank == 0 else None
 
-        def parts(r):
-            U = ranges[r][1] - ranges[r][0]
-            cut = [U * i // GATHER_PARTS for i in range(GATHER_PARTS + 1)]
-            return [(cut[i], cut[i + 1]) for i in range(GATHER_PARTS)]
+        parts = sharding.split_parts(ranges, GATHER_PARTS)
 
         def step(i):
             works = []
-            for part in range(GATHER_PARTS):
-                a, b = parts(rank)[part]
+            for pieces, offs in parts:
+                a, b = pieces[rank]
                 if b > a:
                     block_sparse_attention(q[:, a:b], k[:, a:b], v[:, a:b], plan=run.plan, out=o[:, a:b],
                                            kernel=run.kernel)
-                sizes = [parts(r)[part] for r in range(world)]
-                offs = [ranges[r][0] + sizes[r][0] for r in range(world)]
-                _, w = sharding.gather_units(o[0, a:b], sizes, dst=0, async_op=True, out=full, offsets=offs)
+                _, w = sharding.gather_units(o[0, a:b], pieces, dst=0, async_op=True, out=full, offsets=offs)
                 works += w
             for w in works:
                 w.wait()

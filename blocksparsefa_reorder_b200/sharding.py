@@ -63,6 +63,28 @@ def local_heads(H: int, rank: int, world_size: int) -> tuple:
     return partition_units(H, world_size)[rank]
 
 
+def split_parts(ranges: Sequence[tuple], parts: int) -> list:
+    """Cut every rank's unit range into ``parts`` consecutive pieces (some
+    empty when a rank has fewer units than parts), so that a rank can compute
+    and ship its units piece by piece.  Returns one ``(pieces, offsets)`` per
+    part: ``pieces[r] = (a, b)`` indexes rank r's local units, ``offsets[r]``
+    is the global index of the piece's first unit (``gather_units``'s
+    ``ranges`` / ``offsets`` for that part).  Every rank derives the same
+    list, so all take the same collective steps."""
+    if parts <= 0:
+        raise ValueError("parts must be positive")
+    out = []
+    for i in range(parts):
+        pieces, offsets = [], []
+        for lo, hi in ranges:
+            u = hi - lo
+            a, b = u * i // parts, u * (i + 1) // parts
+            pieces.append((a, b))
+            offsets.append(lo + a)
+        out.append((pieces, offsets))
+    return out
+
+
 def _global_rank(group, r: int) -> int:
     """Global rank of rank ``r`` of ``group`` (point-to-point calls take global ranks)."""
     return r if group is None else dist.get_global_rank(group, r)

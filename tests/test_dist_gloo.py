@@ -105,6 +105,45 @@ def test_gather_over_subgroup(tmp_path):
     assert (tmp_path / "sub.txt").read_text() == "ok"
 
 
+def _worker_parts(rank, world, port, out_dir):
+    """The long-context step's gather: each rank ships its units in 4 parts
+    (rank 0 has fewer units than parts, so some of its pieces are empty), all
+    parts posted before any is waited on; rank 0 must end with every unit at
+    its global index."""
+    try:
+        _init(rank, world, port)
+        ranges = [(0, 3), (3, 8)]
+        lo, hi = ranges[rank]
+        local = torch.arange(lo * 2, hi * 2, dtype=torch.float32).reshape(hi - lo, 2)
+        full = torch.full((8, 2), -1.0) if rank == 0 else None
+        works = []
+        for pieces, offsets in sharding.split_parts(ranges, 4):
+            a, b = pieces[rank]
+            _, w = sharding.gather_units(local[a:b], pieces, dst=0, async_op=True, out=full, offsets=offsets)
+            works += w
+        for w in works:
+            w.wait()
+        if rank == 0:
+            ok = torch.equal(full, torch.arange(16, dtype=torch.float32).reshape(8, 2))
+            with open(os.path.join(out_dir, "parts.txt"), "w") as f:
+                f.write("ok" if ok else "mismatch")
+        dist.barrier()
+        dist.destroy_process_group()
+    except Exception:
+        with open(os.path.join(out_dir, f"fail{rank}.txt"), "w") as f:
+            f.write(traceback.format_exc())
+        raise
+
+
+def test_gather_in_parts(tmp_path):
+    assert sharding.split_parts([(0, 3), (3, 8)], 4) == [
+        ([(0, 0), (0, 1)], [0, 3]), ([(0, 1), (1, 2)], [0, 4]), ([(1, 2), (2, 3)], [1, 5]),
+        ([(2, 3), (3, 5)], [2, 6])]
+    port = _free_port()
+    mp.start_processes(_worker_parts, args=(2, port, str(tmp_path)), nprocs=2, join=True, start_method="spawn")
+    assert (tmp_path / "parts.txt").read_text() == "ok"
+
+
 def _worker_fail(rank, world, port, out_dir):
     _init(rank, world, port, timeout_s=5)
     if rank == 1:
