@@ -74,10 +74,14 @@ NCU_TRAFFIC = {
     "headline": (249925376.0, "ncu --set full --clock-control none -k regex:attn_tcp -s 3 -c 1 python bench.py "
                               "--steps 10 --warmup 3 --no-cpu-baseline --no-per-config --sustained-seconds 0 "
                               "(headline workload)"),
-    "sweep_p20": (4043484160.0, "ncu --set full --clock-control none -k regex:attn_tcp -s 24 -c 2 python bench.py "
+    "sweep_p20": (4038844416.0, "ncu --set full --clock-control none -k regex:attn_tcp -s 24 -c 2 python bench.py "
                                 "--workload sweep_p20 --units 8 --steps 5 --warmup 3 --no-cpu-baseline "
-                                "--no-per-config --sustained-seconds 0, DRAM bytes of the 8-unit launch x 16 "
-                                "(the 128 units are independent)"),
+                                "--no-per-config --sustained-seconds 0 --no-backward --no-gpu-comparator, DRAM bytes "
+                                "of the 8-unit launch x 16 (the 128 units are independent)"),
+    "sweep_p01": (4005896192.0, "ncu --set full --clock-control none -k regex:attn_tcp -s 24 -c 2 python bench.py "
+                                "--workload sweep_p01 --units 8 --steps 5 --warmup 3 --no-cpu-baseline "
+                                "--no-per-config --sustained-seconds 0 --no-backward --no-gpu-comparator, DRAM bytes "
+                                "of the 8-unit launch x 16 (the 128 units are independent)"),
 }
 
 
