@@ -10,7 +10,7 @@ with the coordinates moved to their new positions (``update_idx_perm`` fused
 into the mask build, ``main.py:27-49, 54-63``), then time the forward with
 and without reordering and print the reference runner's lines
 (``run_experiments_B200``).  The reference's other modes run its comparator
-backends (BSFA, FlexAttention, its Triton kernels), which this build does not
+backends (BSFA, FlexAttention, its Triton kernels), which this library does not
 include.  Deliberate difference: ``--num-heads`` may exceed 1 (the kernels
 take any number of heads; the reference refuses values other than 1).
 """
@@ -50,7 +50,7 @@ def parse_args(argv: Optional[list] = None):
     if ns.matrix_mtx.suffix.lower() != ".mtx":
         p.error("Input matrix file must have .mtx extension.")
     if ns.mode in REFERENCE_MODES:
-        p.error(f"--mode {ns.mode} runs one of the reference's comparator backends, which this build does not "
+        p.error(f"--mode {ns.mode} runs one of the reference's comparator backends, which this library does not "
                 "include; use --mode B200")
     if ns.block_size not in (64, 128):
         p.error("--block-size must be 64 or 128 for the B200 kernels.")
